@@ -1,0 +1,123 @@
+// Host-side launch interface of the decode kernels. No torch types; plain
+// device pointers. All launches go on the caller's stream and, when `pdl` is
+// set, carry programmatic stream serialization so a kernel's weight prefetch
+// overlaps the tail of the kernel before it.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mmc {
+
+// Error codes a kernel can leave in the context's device error word.
+enum DeviceError : int {
+  kDevOk = 0,
+  kDevWaitTimeout = 1,    // a bounded mbarrier wait gave up
+  kDevBadToken = 2,       // token id outside [0, vocab)
+  kDevNoPage = 3,         // KV position not backed by a reserved page
+  kDevPositionLimit = 4,  // position >= max_position_embeddings
+};
+
+// Prologue: how a projection kernel builds its input rows x[b][0..K).
+enum Prologue : int {
+  kProPlain = 0,      // x = in[b]                              (fp32 activations)
+  kProNorm = 1,       // x = in[b] * (rs * w)                   decoder_layer.cpp:32-42
+  kProNormFinal = 2,  // x = (in[b] * rs) * w                   language_model.cpp:24-38
+  kProEmbedNorm = 3,  // in[b] = embed[token[b]] (also written to `hidden`), then kProNorm
+};
+
+// Epilogue: what a projection kernel does with y[b][n] = W[n] . x[b].
+enum Epilogue : int {
+  kEpiStore = 0,   // out[b][n] = y
+  kEpiResid = 1,   // out[b][n] += y               (residual stream, fp32)
+  kEpiSwiglu = 2,  // out[b][i] = silu(gate_i) * up_i   (gate/up rows interleaved by 8)
+  kEpiArgmax = 3,  // next token = first argmax_n y (optionally logits[b][n] = y)
+};
+
+// Per-step bookkeeping the lm_head argmax epilogue updates once the next
+// token is known (device-resident decode loop).
+struct TokenSink {
+  int* tokens = nullptr;          // [B] in: this step's tokens; out: next tokens (feedback)
+  int* next_out = nullptr;        // [B] optional copy of the next tokens
+  int* seq_pos = nullptr;         // [max_seqs] position (cached tokens) per sequence slot, += 1
+  const int* slots = nullptr;     // [B] sequence slot of each batch row
+  int* hist = nullptr;            // optional [hist_cap][B] token history
+  int* hist_step = nullptr;       // device counter of history rows written
+  int hist_cap = 0;
+};
+
+struct ProjArgs {
+  const __half* W = nullptr;  // [N][K] row-major fp16
+  int N = 0, K = 0, B = 0;
+  // prologue
+  const float* in = nullptr;  // [B][K] fp32 (hidden / activations)
+  const float* norm_w = nullptr;
+  float eps = 0.f;
+  const float* embed = nullptr;  // [vocab][K] fp32
+  int vocab = 0;
+  const int* tokens = nullptr;
+  float* hidden = nullptr;  // kProEmbedNorm writes the embedding rows here
+  // epilogue
+  float* out = nullptr;  // [B][ldo]
+  int ldo = 0;
+  float* logits = nullptr;  // kEpiArgmax: optional [B][N]
+  void* argmax_part = nullptr;  // kEpiArgmax scratch: [B][grid] (value, index)
+  unsigned* counter = nullptr;  // kEpiArgmax: zero-initialised arrival counter
+  TokenSink sink;
+  int* err = nullptr;
+};
+
+// CUDA-core projection for small batches (B <= 4): each CTA bulk-copies its
+// contiguous weight slab into shared memory before waiting on the previous
+// kernel, then computes all B rows from shared memory.
+int gemv_rows_per_cta(int N, int K, int epi, int num_sms);
+size_t gemv_smem_bytes(int rows_per_cta, int K, int B);
+size_t gemv_argmax_part_bytes(int N, int K, int B, int num_sms);
+cudaError_t launch_gemv(int pro, int epi, const ProjArgs& a, int num_sms, cudaStream_t stream, bool pdl);
+cudaError_t gemv_init_attributes();
+
+// Tensor-core projection for batches B > 4 (mma.sync m16n8k16, fp16 inputs,
+// fp32 accumulate): weights on the M side, batch on N.
+size_t gemm_argmax_part_bytes(int N, int B);
+cudaError_t launch_gemm(int pro, int epi, const ProjArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t gemm_init_attributes();
+
+// Fused decode attention: q/k per-head RMSNorm + rotate-half RoPE, K/V append
+// into the paged cache, split-KV GQA flash-decode over the cache, split
+// combine. One launch per layer.
+struct AttnArgs {
+  const float* qkv = nullptr;  // [B][(nq + 2 nkv) * hd] raw projections (fp32)
+  int ld_qkv = 0;
+  const float* q_norm = nullptr;
+  const float* k_norm = nullptr;
+  const float* rope_cos = nullptr;  // [max_pos][hd/2]
+  const float* rope_sin = nullptr;
+  int max_pos = 0;
+  float eps = 0.f;
+  __half* kv_pool = nullptr;  // pages [n_pages][layers][2][nkv][page][hd] (fp16, swizzled rows)
+  int layer = 0, layers = 0;
+  const int* block_table = nullptr;  // [max_seqs][max_pages]
+  int max_pages = 0;
+  const int* seq_pos = nullptr;  // [max_seqs] tokens cached before this step
+  const int* slots = nullptr;    // [B]
+  int B = 0, nq = 0, nkv = 0, hd = 0;
+  int split_tokens = 0;  // multiple of the page size
+  int max_splits = 0;    // grid.x
+  float* out = nullptr;  // [B][nq * hd] fp32
+  float* part = nullptr;  // [B][nkv][max_splits][rep][hd + 2] split partials
+  unsigned* counters = nullptr;  // [B][nkv], zero-initialised, self-resetting
+  int* err = nullptr;
+};
+constexpr int kPageTokens = 64;
+size_t attn_part_floats(int B, int nkv, int max_splits, int rep, int hd);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t attention_init_attributes();
+
+// Weight packing: fp32 source rows -> fp16 destination rows (RNE), with an
+// optional gate/up interleave by blocks of 8 rows.
+cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s);
+cudaError_t launch_pack_gate_up(const float* gate, const float* up, __half* dst, int64_t inter, int64_t cols,
+                                cudaStream_t s);
+
+}  // namespace mmc

@@ -1,0 +1,49 @@
+// Weight packing at load time: fp32 rows from weights.bin -> fp16 rows in HBM.
+//
+// The reference packs its device weights transposed ([K][N]) for the Cube
+// unit and rounds half away from zero (ascend_matmul.cpp:28-61, 285-305). Here
+// rows stay row-major [N][K] — a decode projection streams each weight row once
+// and contiguous rows give contiguous slabs — and rounding is IEEE
+// round-to-nearest-even (__float2half_rn).
+//
+// gate/up are fused like the reference's gate_up_proj (language_model.cpp:95-119)
+// but interleaved in blocks of 8 rows: packed rows [16j, 16j+8) are gate rows
+// [8j, 8j+8) and packed rows [16j+8, 16j+16) the matching up rows, so the
+// SiLU*mul epilogue finds gate_i and up_i 8 rows apart inside one 16-row tile.
+#include "kernels.h"
+
+namespace mmc {
+namespace {
+
+__global__ void pack_rows_kernel(const float* __restrict__ src, __half* __restrict__ dst, int64_t n) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    dst[i] = __float2half_rn(src[i]);
+}
+
+__global__ void pack_gate_up_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                    __half* __restrict__ dst, int64_t inter, int64_t cols) {
+  const int64_t n = 2 * inter * cols;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t prow = i / cols, c = i % cols;
+    const int64_t blk = prow / 16, r = prow % 16;
+    const int64_t src_row = blk * 8 + (r & 7);
+    const float* s = r < 8 ? gate : up;
+    dst[i] = __float2half_rn(s[src_row * cols + c]);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s) {
+  pack_rows_kernel<<<1184, 256, 0, s>>>(src, dst, rows * cols);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_gate_up(const float* gate, const float* up, __half* dst, int64_t inter, int64_t cols,
+                                cudaStream_t s) {
+  if (inter % 8 != 0) return cudaErrorInvalidValue;
+  pack_gate_up_kernel<<<1184, 256, 0, s>>>(gate, up, dst, inter, cols);
+  return cudaGetLastError();
+}
+
+}  // namespace mmc

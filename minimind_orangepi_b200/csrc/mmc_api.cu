@@ -1,0 +1,1045 @@
+// libminimind_cuda.so: context, weights, paged KV cache and the decode step
+// behind the C ABI declared in include/minimind_cuda.h.
+//
+// One decode step for B rows is a fixed chain of kernels on one stream
+// (5 per layer + 1), every launch after the first carrying programmatic
+// stream serialization so each kernel's weight / KV-page prefetch overlaps its
+// predecessor:
+//   per layer: qkv projection (RMSNorm prologue; layer 0 gathers the embedding)
+//              -> fused attention (q/k norm, RoPE, KV append, flash-decode)
+//              -> o projection (+ residual)
+//              -> gate/up projection (RMSNorm prologue, SiLU*mul epilogue)
+//              -> down projection (+ residual)
+//   lm_head projection (final RMSNorm prologue, argmax epilogue; writes the
+//   next tokens back into the token buffer and advances the positions)
+// B <= 4 uses the CUDA-core projections (gemv.cu), larger batches the
+// tensor-core ones (gemm_mma.cu). The chain can be captured once as a CUDA
+// graph and replayed with the tokens fed back on the device.
+#include "../../include/minimind_cuda.h"
+#include "kernels/kernels.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_error;
+
+struct MmcError : std::runtime_error {
+  int code;
+  MmcError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw MmcError(code, msg); }
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(MMC_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    return MMC_OK;
+  } catch (const MmcError& e) {
+    g_error = e.what();
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_error = "host allocation failed";
+    return MMC_ERR_CUDA;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return MMC_ERR_CUDA;
+  }
+}
+
+template <typename T>
+T* dalloc(size_t count, const char* what) {
+  void* p = nullptr;
+  ck(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)), what);
+  ck(cudaMemset(p, 0, std::max<size_t>(count, 1) * sizeof(T)), what);
+  return static_cast<T*>(p);
+}
+
+struct Layer {
+  float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  __half *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+};
+
+}  // namespace
+
+struct mmc_ctx {
+  mmc_model_desc d{};
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+
+  // weights
+  bool loaded = false;
+  float* embed = nullptr;
+  __half* lm_head = nullptr;
+  float* final_norm = nullptr;
+  std::vector<Layer> layers;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+
+  // KV cache
+  bool kv_ready = false;
+  __half* kv_pool = nullptr;
+  int64_t n_pages = 0, page_halves = 0;
+  int max_seqs = 0, max_pages = 0, max_batch = 0;
+  int* d_block_table = nullptr;
+  int* d_seq_pos = nullptr;
+  std::vector<int> h_block_table;
+  std::vector<int64_t> h_pos;
+  std::vector<int> h_pages;  // pages reserved per sequence
+  std::vector<char> h_open;
+  std::vector<int> free_pages;
+
+  // per-step scratch (sized for max_batch)
+  float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+  int *tokens = nullptr, *slots = nullptr, *next = nullptr;
+  void* argmax_part = nullptr;
+  unsigned* argmax_counter = nullptr;
+  float* attn_part = nullptr;
+  unsigned* attn_counters = nullptr;
+  int* err = nullptr;
+  int* h_stage = nullptr;  // pinned: [2][max_batch] ints
+  int max_splits_cap = 64;
+  std::vector<int> async_slots;  // slot list currently in `slots` for mmc_decode_step_async
+
+  // graph loop
+  cudaGraphExec_t graph = nullptr;
+  int graph_batch = 0;
+  std::vector<int> graph_slots;
+  int* hist = nullptr;
+  int* hist_step = nullptr;
+  int hist_cap = 0;
+
+  template <typename T>
+  T* alloc(size_t n, const char* what) {
+    T* p = dalloc<T>(n, what);
+    allocs.push_back(p);
+    return p;
+  }
+  int q_size() const { return int(d.num_attention_heads * d.head_dim); }
+  int kv_size() const { return int(d.num_key_value_heads * d.head_dim); }
+  int rep() const { return int(d.num_attention_heads / d.num_key_value_heads); }
+};
+
+namespace {
+
+void use_device(const mmc_ctx* c) { ck(cudaSetDevice(c->device), "cudaSetDevice"); }
+
+void require(bool ok, int code, const std::string& msg) {
+  if (!ok) fail(code, msg);
+}
+
+void check_device_error(mmc_ctx* c) {
+  int e = 0;
+  ck(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+  if (e != 0) {
+    ck(cudaMemset(c->err, 0, sizeof(int)), "clear device error word");
+    const char* what = e == mmc::kDevWaitTimeout   ? "a bounded wait timed out"
+                       : e == mmc::kDevBadToken    ? "token id out of vocabulary range"
+                       : e == mmc::kDevNoPage      ? "KV position not backed by a reserved page"
+                       : e == mmc::kDevPositionLimit ? "position exceeds max_position_embeddings"
+                                                     : "unknown";
+    fail(MMC_ERR_DEVICE, std::string("device error: ") + what);
+  }
+}
+
+// Split size for the attention kernel: enough CTAs to cover the SMs a few
+// times over, at most `max_splits_cap` splits per sequence.
+int plan_split(const mmc_ctx* c, int64_t total_pages, int64_t max_ctx, int* max_splits) {
+  const int64_t pages = std::max<int64_t>(1, (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens);
+  int64_t sp = std::max<int64_t>(1, total_pages * c->d.num_key_value_heads / (4 * c->num_sms));
+  sp = std::max<int64_t>(sp, (pages + c->max_splits_cap - 1) / c->max_splits_cap);
+  sp = std::min<int64_t>(sp, pages);
+  *max_splits = int((pages + sp - 1) / sp);
+  return int(sp * mmc::kPageTokens);
+}
+
+struct StepIO {
+  int B = 0;
+  const int* slots = nullptr;
+  int* tokens = nullptr;
+  int* next_out = nullptr;
+  float* logits = nullptr;
+  int* hist = nullptr;
+  int* hist_step = nullptr;
+  int hist_cap = 0;
+  int split_tokens = 64;
+  int max_splits = 1;
+};
+
+int kernels_per_step(const mmc_ctx* c) { return int(c->d.num_hidden_layers) * 5 + 1; }
+
+void launch_proj(mmc_ctx* c, int pro, int epi, const mmc::ProjArgs& a, cudaStream_t s, bool pdl) {
+  cudaError_t e = a.B <= 4 ? mmc::launch_gemv(pro, epi, a, c->num_sms, s, pdl) : mmc::launch_gemm(pro, epi, a, s, pdl);
+  ck(e, "projection launch");
+}
+
+void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
+  const auto& d = c->d;
+  const int H = int(d.hidden_size), I = int(d.intermediate_size), Q = c->q_size(), KV = c->kv_size();
+  const int NQKV = Q + 2 * KV;
+  bool pdl = false;
+  for (int l = 0; l < int(d.num_hidden_layers); ++l) {
+    const Layer& L = c->layers[l];
+    mmc::ProjArgs p;
+    p.B = io.B;
+    p.err = c->err;
+    // qkv
+    p.W = L.qkv;
+    p.N = NQKV;
+    p.K = H;
+    p.in = c->hidden;
+    p.norm_w = L.in_norm;
+    p.eps = d.rms_norm_eps;
+    p.out = c->qkv;
+    p.ldo = NQKV;
+    if (l == 0) {
+      p.embed = c->embed;
+      p.vocab = int(d.vocab_size);
+      p.tokens = io.tokens;
+      p.hidden = c->hidden;
+    }
+    launch_proj(c, l == 0 ? mmc::kProEmbedNorm : mmc::kProNorm, mmc::kEpiStore, p, s, pdl);
+    pdl = true;
+    // attention
+    mmc::AttnArgs a;
+    a.qkv = c->qkv;
+    a.ld_qkv = NQKV;
+    a.q_norm = L.q_norm;
+    a.k_norm = L.k_norm;
+    a.rope_cos = c->rope_cos;
+    a.rope_sin = c->rope_sin;
+    a.max_pos = int(d.max_position_embeddings);
+    a.eps = d.rms_norm_eps;
+    a.kv_pool = c->kv_pool;
+    a.layer = l;
+    a.layers = int(d.num_hidden_layers);
+    a.block_table = c->d_block_table;
+    a.max_pages = c->max_pages;
+    a.seq_pos = c->d_seq_pos;
+    a.slots = io.slots;
+    a.B = io.B;
+    a.nq = int(d.num_attention_heads);
+    a.nkv = int(d.num_key_value_heads);
+    a.hd = int(d.head_dim);
+    a.split_tokens = io.split_tokens;
+    a.max_splits = io.max_splits;
+    a.out = c->attn;
+    a.part = c->attn_part;
+    a.counters = c->attn_counters;
+    a.err = c->err;
+    ck(mmc::launch_attention(a, s, pdl), "attention launch");
+    // o projection + residual
+    mmc::ProjArgs o;
+    o.B = io.B;
+    o.err = c->err;
+    o.W = L.o;
+    o.N = H;
+    o.K = Q;
+    o.in = c->attn;
+    o.out = c->hidden;
+    o.ldo = H;
+    launch_proj(c, mmc::kProPlain, mmc::kEpiResid, o, s, pdl);
+    // gate/up + SiLU*mul
+    mmc::ProjArgs gu;
+    gu.B = io.B;
+    gu.err = c->err;
+    gu.W = L.gu;
+    gu.N = 2 * I;
+    gu.K = H;
+    gu.in = c->hidden;
+    gu.norm_w = L.post_norm;
+    gu.eps = d.rms_norm_eps;
+    gu.out = c->act;
+    gu.ldo = I;
+    launch_proj(c, mmc::kProNorm, mmc::kEpiSwiglu, gu, s, pdl);
+    // down + residual
+    mmc::ProjArgs dn;
+    dn.B = io.B;
+    dn.err = c->err;
+    dn.W = L.down;
+    dn.N = H;
+    dn.K = I;
+    dn.in = c->act;
+    dn.out = c->hidden;
+    dn.ldo = H;
+    launch_proj(c, mmc::kProPlain, mmc::kEpiResid, dn, s, pdl);
+  }
+  // final norm + lm_head + argmax
+  mmc::ProjArgs lm;
+  lm.B = io.B;
+  lm.err = c->err;
+  lm.W = c->lm_head;
+  lm.N = int(d.vocab_size);
+  lm.K = H;
+  lm.in = c->hidden;
+  lm.norm_w = c->final_norm;
+  lm.eps = d.rms_norm_eps;
+  lm.logits = io.logits;
+  lm.argmax_part = c->argmax_part;
+  lm.counter = c->argmax_counter;
+  lm.sink.tokens = io.tokens;
+  lm.sink.next_out = io.next_out;
+  lm.sink.seq_pos = c->d_seq_pos;
+  lm.sink.slots = io.slots;
+  lm.sink.hist = io.hist;
+  lm.sink.hist_step = io.hist_step;
+  lm.sink.hist_cap = io.hist_cap;
+  launch_proj(c, mmc::kProNormFinal, mmc::kEpiArgmax, lm, s, true);
+}
+
+void require_ready(const mmc_ctx* c) {
+  require(c != nullptr, MMC_ERR_INVALID, "null context");
+  require(c->loaded, MMC_ERR_STATE, "weights are not loaded");
+  require(c->kv_ready, MMC_ERR_STATE, "KV cache is not initialised (mmc_kv_init)");
+}
+
+void check_seq(const mmc_ctx* c, int32_t seq) {
+  require(seq >= 0 && seq < c->max_seqs && c->h_open[seq], MMC_ERR_INVALID, "invalid sequence id");
+}
+
+void reserve_pages(mmc_ctx* c, int32_t seq, int64_t tokens) {
+  require(tokens <= c->d.max_position_embeddings, MMC_ERR_OUT_OF_RANGE,
+          "reservation exceeds max_position_embeddings");
+  const int need = int((tokens + mmc::kPageTokens - 1) / mmc::kPageTokens);
+  require(need <= c->max_pages, MMC_ERR_INVALID, "reservation exceeds the per-sequence page table");
+  int have = c->h_pages[seq];
+  if (need <= have) return;
+  require(int64_t(c->free_pages.size()) >= need - have, MMC_ERR_NO_PAGES, "KV page pool exhausted");
+  for (; have < need; ++have) {
+    c->h_block_table[size_t(seq) * c->max_pages + have] = c->free_pages.back();
+    c->free_pages.pop_back();
+  }
+  const int old = c->h_pages[seq];
+  c->h_pages[seq] = need;
+  ck(cudaMemcpy(c->d_block_table + size_t(seq) * c->max_pages + old,
+                c->h_block_table.data() + size_t(seq) * c->max_pages + old, sizeof(int) * (need - old),
+                cudaMemcpyHostToDevice),
+     "block table upload");
+}
+
+// Host-side checks shared by the eager step entry points; returns the plan.
+StepIO plan_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, bool auto_reserve) {
+  require_ready(c);
+  require(batch >= 1 && batch <= c->max_batch, MMC_ERR_INVALID, "batch outside [1, max_batch]");
+  require(seq_ids != nullptr, MMC_ERR_INVALID, "null seq_ids");
+  std::vector<char> seen(c->max_seqs, 0);
+  int64_t total_pages = 0, max_ctx = 1;
+  for (int b = 0; b < batch; ++b) {
+    const int32_t s = seq_ids[b];
+    check_seq(c, s);
+    require(!seen[s], MMC_ERR_INVALID, "a sequence appears twice in one batch");
+    seen[s] = 1;
+    const int64_t ctx = c->h_pos[s] + 1;
+    require(ctx <= c->d.max_position_embeddings, MMC_ERR_OUT_OF_RANGE, "position exceeds max_position_embeddings");
+    if (auto_reserve) reserve_pages(c, s, ctx);
+    require(int64_t(c->h_pages[s]) * mmc::kPageTokens >= ctx, MMC_ERR_NO_PAGES, "sequence has no page for this position");
+    total_pages += (ctx + mmc::kPageTokens - 1) / mmc::kPageTokens;
+    max_ctx = std::max(max_ctx, ctx);
+  }
+  StepIO io;
+  io.B = batch;
+  io.split_tokens = plan_split(c, total_pages, max_ctx, &io.max_splits);
+  return io;
+}
+
+std::vector<float> rope_table(int64_t max_pos, int64_t hd, float theta, bool want_sin) {
+  // decoder_layer.cpp:97-122: inv_freq = 1 / theta^(2d/hd), angle = pos * inv_freq,
+  // evaluated in fp32 with the same float math calls so the table is bit-equal.
+  const int64_t half = hd / 2;
+  std::vector<float> t(size_t(max_pos * half));
+  for (int64_t p = 0; p < max_pos; ++p)
+    for (int64_t j = 0; j < half; ++j) {
+      const float inv_freq = 1.0F / std::pow(theta, static_cast<float>(j * 2) / static_cast<float>(hd));
+      const float angle = static_cast<float>(p) * inv_freq;
+      t[size_t(p * half + j)] = want_sin ? std::sin(angle) : std::cos(angle);
+    }
+  return t;
+}
+
+const char* tensor_suffix(int i) {
+  static const char* names[] = {"input_layernorm.weight",    "post_attention_layernorm.weight",
+                                "self_attn.q_norm.weight",   "self_attn.k_norm.weight",
+                                "self_attn.q_proj.weight",   "self_attn.k_proj.weight",
+                                "self_attn.v_proj.weight",   "self_attn.o_proj.weight",
+                                "mlp.gate_proj.weight",      "mlp.up_proj.weight",
+                                "mlp.down_proj.weight"};
+  return names[i];
+}
+
+// expected element count of tensor i in weights.bin order
+int64_t expected_count(const mmc_model_desc& d, int i) {
+  const int64_t H = d.hidden_size, V = d.vocab_size, Q = d.num_attention_heads * d.head_dim,
+                KV = d.num_key_value_heads * d.head_dim, I = d.intermediate_size, HD = d.head_dim;
+  if (i == 0 || i == 2) return V * H;
+  if (i == 1) return H;
+  const int j = (i - 3) % 11;
+  const int64_t counts[11] = {H, H, HD, HD, Q * H, KV * H, KV * H, H * Q, I * H, I * H, H * I};
+  return counts[j];
+}
+
+std::string tensor_name(const mmc_model_desc&, int i) {
+  if (i == 0) return "model.embed_tokens.weight";
+  if (i == 1) return "model.norm.weight";
+  if (i == 2) return "lm_head.weight";
+  return "model.layers." + std::to_string((i - 3) / 11) + "." + tensor_suffix((i - 3) % 11);
+}
+
+// Upload all tensors; `get(i, staging)` fills host fp32 tensor i.
+template <typename Getter>
+void upload_weights(mmc_ctx* c, Getter&& get) {
+  const auto& d = c->d;
+  const int64_t H = d.hidden_size, V = d.vocab_size, Q = c->q_size(), KV = c->kv_size(), I = d.intermediate_size;
+  const int n = 3 + 11 * int(d.num_hidden_layers);
+  int64_t max_count = 0;
+  for (int i = 0; i < n; ++i) max_count = std::max(max_count, expected_count(d, i));
+  float* stage_d = nullptr;
+  ck(cudaMalloc(&stage_d, size_t(max_count) * 4 * 2), "weight staging");
+  std::unique_ptr<float, void (*)(float*)> guard(stage_d, [](float* p) { cudaFree(p); });
+  float* stage_d2 = stage_d + max_count;
+  std::vector<float> host, host2;
+  auto put = [&](int i, float* dst_d) {
+    get(i, host);
+    ck(cudaMemcpy(dst_d, host.data(), host.size() * 4, cudaMemcpyHostToDevice), "weight upload");
+  };
+  c->embed = c->alloc<float>(size_t(V * H), "embed");
+  put(0, c->embed);
+  c->final_norm = c->alloc<float>(size_t(H), "final_norm");
+  put(1, c->final_norm);
+  c->lm_head = c->alloc<__half>(size_t(V * H), "lm_head");
+  put(2, stage_d);
+  ck(mmc::launch_pack_rows(stage_d, c->lm_head, V, H, c->stream), "pack lm_head");
+  ck(cudaStreamSynchronize(c->stream), "pack");
+  c->layers.assign(size_t(d.num_hidden_layers), Layer{});
+  for (int l = 0; l < int(d.num_hidden_layers); ++l) {
+    Layer& L = c->layers[l];
+    const int base = 3 + 11 * l;
+    L.in_norm = c->alloc<float>(size_t(H), "norm");
+    put(base + 0, L.in_norm);
+    L.post_norm = c->alloc<float>(size_t(H), "norm");
+    put(base + 1, L.post_norm);
+    L.q_norm = c->alloc<float>(size_t(d.head_dim), "norm");
+    put(base + 2, L.q_norm);
+    L.k_norm = c->alloc<float>(size_t(d.head_dim), "norm");
+    put(base + 3, L.k_norm);
+    // fused [q; k; v] rows, language_model.cpp:95-119
+    L.qkv = c->alloc<__half>(size_t((Q + 2 * KV) * H), "qkv");
+    put(base + 4, stage_d);
+    ck(mmc::launch_pack_rows(stage_d, L.qkv, Q, H, c->stream), "pack q");
+    ck(cudaStreamSynchronize(c->stream), "pack");
+    put(base + 5, stage_d);
+    ck(mmc::launch_pack_rows(stage_d, L.qkv + Q * H, KV, H, c->stream), "pack k");
+    ck(cudaStreamSynchronize(c->stream), "pack");
+    put(base + 6, stage_d);
+    ck(mmc::launch_pack_rows(stage_d, L.qkv + (Q + KV) * H, KV, H, c->stream), "pack v");
+    ck(cudaStreamSynchronize(c->stream), "pack");
+    L.o = c->alloc<__half>(size_t(H * Q), "o");
+    put(base + 7, stage_d);
+    ck(mmc::launch_pack_rows(stage_d, L.o, H, Q, c->stream), "pack o");
+    ck(cudaStreamSynchronize(c->stream), "pack");
+    L.gu = c->alloc<__half>(size_t(2 * I * H), "gate_up");
+    put(base + 8, stage_d);
+    put(base + 9, stage_d2);
+    ck(mmc::launch_pack_gate_up(stage_d, stage_d2, L.gu, I, H, c->stream), "pack gate_up");
+    ck(cudaStreamSynchronize(c->stream), "pack");
+    L.down = c->alloc<__half>(size_t(H * I), "down");
+    put(base + 10, stage_d);
+    ck(mmc::launch_pack_rows(stage_d, L.down, H, I, c->stream), "pack down");
+    ck(cudaStreamSynchronize(c->stream), "pack");
+  }
+  const auto cos_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, false);
+  const auto sin_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, true);
+  c->rope_cos = c->alloc<float>(cos_t.size(), "rope");
+  c->rope_sin = c->alloc<float>(sin_t.size(), "rope");
+  ck(cudaMemcpy(c->rope_cos, cos_t.data(), cos_t.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+  ck(cudaMemcpy(c->rope_sin, sin_t.data(), sin_t.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+  c->loaded = true;
+}
+
+void drop_graph(mmc_ctx* c) {
+  if (c->graph) cudaGraphExecDestroy(c->graph);
+  c->graph = nullptr;
+  c->graph_batch = 0;
+  c->graph_slots.clear();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mmc_last_error(void) { return g_error.c_str(); }
+int mmc_abi_version(void) { return 1; }
+
+int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
+  return guarded([&] {
+    require(desc && out, MMC_ERR_INVALID, "null argument");
+    const mmc_model_desc& d = *desc;
+    require(d.hidden_size > 0 && d.num_hidden_layers > 0 && d.num_attention_heads > 0 &&
+                d.num_key_value_heads > 0 && d.head_dim > 0 && d.intermediate_size > 0 && d.vocab_size > 0 &&
+                d.max_position_embeddings > 0,
+            MMC_ERR_INVALID, "model dimensions must be positive");
+    require(d.num_attention_heads % d.num_key_value_heads == 0, MMC_ERR_INVALID,
+            "num_attention_heads must be divisible by num_key_value_heads");
+    require(d.num_attention_heads / d.num_key_value_heads <= 8, MMC_ERR_INVALID,
+            "at most 8 query heads per kv head are supported");
+    require(d.head_dim == 16 || d.head_dim == 32 || d.head_dim == 64 || d.head_dim == 96 || d.head_dim == 128,
+            MMC_ERR_INVALID, "head_dim must be one of 16, 32, 64, 96, 128");
+    require(d.hidden_size % 64 == 0 && d.intermediate_size % 64 == 0 &&
+                (d.num_attention_heads * d.head_dim) % 64 == 0,
+            MMC_ERR_INVALID, "hidden_size, intermediate_size and heads*head_dim must be multiples of 64");
+    require(d.rms_norm_eps > 0.f && d.rope_theta > 0.f, MMC_ERR_INVALID, "eps and theta must be positive");
+    auto c = std::make_unique<mmc_ctx>();
+    c->d = d;
+    c->device = device;
+    ck(cudaSetDevice(device), "cudaSetDevice");
+    int major = 0;
+    ck(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), "device query");
+    require(major == 10, MMC_ERR_CUDA, "libminimind_cuda is built for sm_100a (B200) only");
+    ck(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device), "device query");
+    ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
+    ck(mmc::gemv_init_attributes(), "gemv attributes");
+    ck(mmc::gemm_init_attributes(), "gemm attributes");
+    ck(mmc::attention_init_attributes(), "attention attributes");
+    c->err = c->alloc<int>(1, "error word");
+    *out = c.release();
+  });
+}
+
+void mmc_destroy(mmc_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  drop_graph(c);
+  for (void* p : c->allocs) cudaFree(p);
+  if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+int mmc_load_weights(mmc_ctx* c, const float* const* tensors, const int64_t* counts, int32_t n) {
+  return guarded([&] {
+    require(c && tensors && counts, MMC_ERR_INVALID, "null argument");
+    require(!c->loaded, MMC_ERR_STATE, "weights already loaded");
+    use_device(c);
+    const int expect = 3 + 11 * int(c->d.num_hidden_layers);
+    require(n == expect, MMC_ERR_INVALID, "expected " + std::to_string(expect) + " tensors in weights.bin order");
+    for (int i = 0; i < n; ++i)
+      require(counts[i] == expected_count(c->d, i) && tensors[i], MMC_ERR_INVALID,
+              tensor_name(c->d, i) + " has invalid size");
+    upload_weights(c, [&](int i, std::vector<float>& h) { h.assign(tensors[i], tensors[i] + counts[i]); });
+  });
+}
+
+int mmc_load_weights_file(mmc_ctx* c, const char* path) {
+  return guarded([&] {
+    require(c && path, MMC_ERR_INVALID, "null argument");
+    require(!c->loaded, MMC_ERR_STATE, "weights already loaded");
+    use_device(c);
+    std::ifstream in(path, std::ios::binary);
+    require(bool(in), MMC_ERR_IO, std::string("failed to open runtime weights: ") + path);
+    char magic[8] = {};
+    in.read(magic, 8);
+    require(bool(in) && std::memcmp(magic, "MMRTW001", 8) == 0, MMC_ERR_IO, "unsupported runtime weight format");
+    int next = 0;
+    upload_weights(c, [&](int i, std::vector<float>& h) {
+      require(i == next++, MMC_ERR_STATE, "weights must be read in file order");
+      uint64_t len = 0;
+      in.read(reinterpret_cast<char*>(&len), 8);
+      require(bool(in) && len < 4096, MMC_ERR_IO, "failed to read tensor name");
+      std::string name(len, '\0');
+      in.read(name.data(), std::streamsize(len));
+      const std::string want = tensor_name(c->d, i);
+      require(bool(in) && name == want, MMC_ERR_IO, "expected tensor " + want + ", got " + name);
+      uint64_t count = 0;
+      in.read(reinterpret_cast<char*>(&count), 8);
+      require(bool(in) && int64_t(count) == expected_count(c->d, i), MMC_ERR_IO, want + " has invalid size");
+      h.resize(count);
+      in.read(reinterpret_cast<char*>(h.data()), std::streamsize(count * 4));
+      require(bool(in), MMC_ERR_IO, "failed to read " + want);
+    });
+  });
+}
+
+int mmc_kv_page_bytes(const mmc_ctx* c, int64_t* bytes) {
+  return guarded([&] {
+    require(c && bytes, MMC_ERR_INVALID, "null argument");
+    *bytes = c->d.num_hidden_layers * 2 * c->d.num_key_value_heads * mmc::kPageTokens * c->d.head_dim * 2;
+  });
+}
+
+int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    require(!c->kv_ready, MMC_ERR_STATE, "KV cache already initialised");
+    require(n_pages > 0 && n_pages < (int64_t(1) << 31) && max_seqs > 0 && max_batch > 0, MMC_ERR_INVALID,
+            "n_pages, max_seqs and max_batch must be positive");
+    use_device(c);
+    const auto& d = c->d;
+    c->page_halves = d.num_hidden_layers * 2 * d.num_key_value_heads * mmc::kPageTokens * d.head_dim;
+    c->n_pages = n_pages;
+    c->max_seqs = max_seqs;
+    c->max_batch = max_batch;
+    c->max_pages = int((d.max_position_embeddings + mmc::kPageTokens - 1) / mmc::kPageTokens);
+    c->kv_pool = c->alloc<__half>(size_t(n_pages) * c->page_halves, "KV page pool");
+    c->d_block_table = c->alloc<int>(size_t(max_seqs) * c->max_pages, "block table");
+    c->d_seq_pos = c->alloc<int>(size_t(max_seqs), "positions");
+    c->h_block_table.assign(size_t(max_seqs) * c->max_pages, -1);
+    ck(cudaMemcpy(c->d_block_table, c->h_block_table.data(), c->h_block_table.size() * 4, cudaMemcpyHostToDevice),
+       "block table init");
+    c->h_pos.assign(size_t(max_seqs), 0);
+    c->h_pages.assign(size_t(max_seqs), 0);
+    c->h_open.assign(size_t(max_seqs), 0);
+    c->free_pages.resize(size_t(n_pages));
+    for (int64_t i = 0; i < n_pages; ++i) c->free_pages[size_t(i)] = int(n_pages - 1 - i);
+    const int H = int(d.hidden_size), I = int(d.intermediate_size), Q = c->q_size(), KV = c->kv_size();
+    const int V = int(d.vocab_size);
+    c->hidden = c->alloc<float>(size_t(max_batch) * H, "hidden");
+    c->qkv = c->alloc<float>(size_t(max_batch) * (Q + 2 * KV), "qkv");
+    c->attn = c->alloc<float>(size_t(max_batch) * Q, "attn");
+    c->act = c->alloc<float>(size_t(max_batch) * I, "act");
+    c->logits = c->alloc<float>(size_t(max_batch) * V, "logits");
+    c->tokens = c->alloc<int>(size_t(max_batch), "tokens");
+    c->slots = c->alloc<int>(size_t(max_batch), "slots");
+    c->next = c->alloc<int>(size_t(max_batch), "next");
+    size_t part_bytes = 0;
+    for (int b = 1; b <= std::min(max_batch, 4); ++b)
+      part_bytes = std::max(part_bytes, mmc::gemv_argmax_part_bytes(V, H, b, c->num_sms));
+    part_bytes = std::max(part_bytes, mmc::gemm_argmax_part_bytes(V, max_batch));
+    c->argmax_part = c->alloc<uint8_t>(part_bytes, "argmax partials");
+    c->argmax_counter = c->alloc<unsigned>(size_t(max_batch) + 2, "argmax counters");
+    c->attn_part = c->alloc<float>(
+        mmc::attn_part_floats(max_batch, int(d.num_key_value_heads), c->max_splits_cap, c->rep(), int(d.head_dim)),
+        "attention partials");
+    c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
+    ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
+    c->kv_ready = true;
+  });
+}
+
+int mmc_seq_open(mmc_ctx* c, int64_t reserve_tokens, int32_t* seq_out) {
+  return guarded([&] {
+    require(c && seq_out, MMC_ERR_INVALID, "null argument");
+    require(c->kv_ready, MMC_ERR_STATE, "KV cache is not initialised (mmc_kv_init)");
+    use_device(c);
+    int s = -1;
+    for (int i = 0; i < c->max_seqs; ++i)
+      if (!c->h_open[i]) {
+        s = i;
+        break;
+      }
+    require(s >= 0, MMC_ERR_NO_PAGES, "all sequence slots are in use");
+    c->h_open[s] = 1;
+    c->h_pos[s] = 0;
+    c->h_pages[s] = 0;
+    const int zero = 0;
+    ck(cudaMemcpy(c->d_seq_pos + s, &zero, sizeof(int), cudaMemcpyHostToDevice), "position reset");
+    try {
+      reserve_pages(c, s, std::max<int64_t>(reserve_tokens, 1));
+    } catch (...) {
+      c->h_open[s] = 0;
+      throw;
+    }
+    *seq_out = s;
+  });
+}
+
+int mmc_seq_reserve(mmc_ctx* c, int32_t seq, int64_t tokens) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    check_seq(c, seq);
+    reserve_pages(c, seq, tokens);
+  });
+}
+
+int mmc_seq_close(mmc_ctx* c, int32_t seq) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    check_seq(c, seq);
+    ck(cudaStreamSynchronize(c->stream), "drain before close");
+    for (int p = 0; p < c->h_pages[seq]; ++p) {
+      int& e = c->h_block_table[size_t(seq) * c->max_pages + p];
+      c->free_pages.push_back(e);
+      e = -1;
+    }
+    if (c->h_pages[seq] > 0)
+      ck(cudaMemcpy(c->d_block_table + size_t(seq) * c->max_pages,
+                    c->h_block_table.data() + size_t(seq) * c->max_pages, sizeof(int) * c->h_pages[seq],
+                    cudaMemcpyHostToDevice),
+         "block table upload");
+    c->h_pages[seq] = 0;
+    c->h_open[seq] = 0;
+    c->h_pos[seq] = 0;
+    if (std::find(c->graph_slots.begin(), c->graph_slots.end(), seq) != c->graph_slots.end()) drop_graph(c);
+  });
+}
+
+int mmc_seq_position(const mmc_ctx* c, int32_t seq, int64_t* pos) {
+  return guarded([&] {
+    require(c && pos, MMC_ERR_INVALID, "null argument");
+    check_seq(c, seq);
+    *pos = c->h_pos[seq];
+  });
+}
+
+int mmc_debug_read_kv(mmc_ctx* c, int32_t seq, int32_t layer, float* keys, float* values) {
+  return guarded([&] {
+    require(c && keys && values, MMC_ERR_INVALID, "null argument");
+    require_ready(c);
+    use_device(c);
+    check_seq(c, seq);
+    require(layer >= 0 && layer < c->d.num_hidden_layers, MMC_ERR_INVALID, "layer out of range");
+    ck(cudaStreamSynchronize(c->stream), "sync");
+    const int hd = int(c->d.head_dim), nkv = int(c->d.num_key_value_heads), cpr = hd / 8;
+    const int64_t tile = int64_t(mmc::kPageTokens) * hd;
+    std::vector<__half> slab(static_cast<size_t>(tile));
+    const int64_t n = c->h_pos[seq];
+    for (int64_t p0 = 0; p0 < n; p0 += mmc::kPageTokens) {
+      const int page = c->h_block_table[size_t(seq) * c->max_pages + p0 / mmc::kPageTokens];
+      for (int kv = 0; kv < 2; ++kv)
+        for (int h = 0; h < nkv; ++h) {
+          const size_t off = ((((size_t)page * c->d.num_hidden_layers + layer) * 2 + kv) * nkv + h) * size_t(tile);
+          ck(cudaMemcpy(slab.data(), c->kv_pool + off, size_t(tile) * 2, cudaMemcpyDeviceToHost), "read page");
+          for (int r = 0; r < mmc::kPageTokens && p0 + r < n; ++r)
+            for (int ch = 0; ch < cpr; ++ch)
+              for (int e = 0; e < 8; ++e) {
+                const __half v = slab[size_t(mmc_kv_row_offset(hd, r, ch) + e)];
+                float* dst = kv ? values : keys;
+                dst[size_t(((p0 + r) * nkv + h) * hd + ch * 8 + e)] = __half2float(v);
+              }
+        }
+    }
+  });
+}
+
+int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int32_t* tokens, int32_t* next_tokens,
+                    float* logits_host) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    require(tokens && next_tokens, MMC_ERR_INVALID, "null argument");
+    StepIO io = plan_step(c, batch, seq_ids, /*auto_reserve=*/true);
+    for (int b = 0; b < batch; ++b)
+      require(tokens[b] >= 0 && tokens[b] < c->d.vocab_size, MMC_ERR_OUT_OF_RANGE,
+              "token id out of vocabulary range");
+    std::memcpy(c->h_stage, seq_ids, sizeof(int) * batch);
+    std::memcpy(c->h_stage + batch, tokens, sizeof(int) * batch);
+    ck(cudaMemcpyAsync(c->slots, c->h_stage, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream), "H2D slots");
+    c->async_slots.clear();
+    ck(cudaMemcpyAsync(c->tokens, c->h_stage + batch, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream),
+       "H2D tokens");
+    io.slots = c->slots;
+    io.tokens = c->tokens;
+    io.logits = logits_host ? c->logits : nullptr;
+    enqueue_step(c, io, c->stream);
+    ck(cudaMemcpyAsync(c->h_stage + 2 * batch, c->tokens, sizeof(int) * batch, cudaMemcpyDeviceToHost, c->stream),
+       "D2H next tokens");
+    if (logits_host)
+      ck(cudaMemcpyAsync(logits_host, c->logits, sizeof(float) * batch * c->d.vocab_size, cudaMemcpyDeviceToHost,
+                         c->stream),
+         "D2H logits");
+    ck(cudaStreamSynchronize(c->stream), "decode step");
+    check_device_error(c);
+    std::memcpy(next_tokens, c->h_stage + 2 * batch, sizeof(int) * batch);
+    for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
+  });
+}
+
+int mmc_decode_step_async(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int32_t* d_tokens,
+                          int32_t* d_next, float* d_logits, void* stream) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    require(d_tokens && d_next, MMC_ERR_INVALID, "null argument");
+    StepIO io = plan_step(c, batch, seq_ids, /*auto_reserve=*/true);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    if (c->async_slots.size() != size_t(batch) || !std::equal(seq_ids, seq_ids + batch, c->async_slots.begin())) {
+      // the slot list changes rarely: upload it synchronously and remember it
+      ck(cudaStreamSynchronize(s), "drain before slot upload");
+      ck(cudaMemcpy(c->slots, seq_ids, sizeof(int) * batch, cudaMemcpyHostToDevice), "H2D slots");
+      c->async_slots.assign(seq_ids, seq_ids + batch);
+    }
+    ck(cudaMemcpyAsync(c->tokens, d_tokens, sizeof(int) * batch, cudaMemcpyDeviceToDevice, s), "tokens");
+    io.slots = c->slots;
+    io.tokens = c->tokens;
+    io.next_out = d_next;
+    io.logits = d_logits;
+    enqueue_step(c, io, s);
+    for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
+  });
+}
+
+int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    require_ready(c);
+    require(batch >= 1 && batch <= c->max_batch && seq_ids, MMC_ERR_INVALID, "bad batch");
+    drop_graph(c);
+    int64_t total_pages = 0, cap = 1;
+    for (int b = 0; b < batch; ++b) {
+      check_seq(c, seq_ids[b]);
+      const int64_t tok = int64_t(c->h_pages[seq_ids[b]]) * mmc::kPageTokens;
+      total_pages += c->h_pages[seq_ids[b]];
+      cap = std::max(cap, tok);
+    }
+    // validation of duplicates etc.
+    (void)plan_step(c, batch, seq_ids, false);
+    StepIO io;
+    io.B = batch;
+    io.split_tokens = plan_split(c, total_pages, cap, &io.max_splits);
+    if (!c->hist) {
+      c->hist_cap = 8192;
+      c->hist = c->alloc<int>(size_t(c->hist_cap) * c->max_batch, "token history");
+      c->hist_step = c->alloc<int>(1, "history counter");
+    }
+    ck(cudaMemcpy(c->slots, seq_ids, sizeof(int) * batch, cudaMemcpyHostToDevice), "slots");
+    c->async_slots.clear();
+    io.slots = c->slots;
+    io.tokens = c->tokens;
+    io.hist = c->hist;
+    io.hist_step = c->hist_step;
+    io.hist_cap = c->hist_cap;
+    cudaGraph_t g = nullptr;
+    ck(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      enqueue_step(c, io, c->stream);
+    } catch (...) {
+      cudaStreamEndCapture(c->stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    ck(cudaStreamEndCapture(c->stream, &g), "end capture");
+    cudaError_t e = cudaGraphInstantiate(&c->graph, g, 0);
+    cudaGraphDestroy(g);
+    ck(e, "graph instantiate");
+    c->graph_batch = batch;
+    c->graph_slots.assign(seq_ids, seq_ids + batch);
+  });
+}
+
+int mmc_graph_set_tokens(mmc_ctx* c, const int32_t* tokens) {
+  return guarded([&] {
+    require(c && tokens && c->graph, MMC_ERR_STATE, "no graph built");
+    use_device(c);
+    for (int b = 0; b < c->graph_batch; ++b)
+      require(tokens[b] >= 0 && tokens[b] < c->d.vocab_size, MMC_ERR_OUT_OF_RANGE, "token id out of vocabulary range");
+    ck(cudaMemcpy(c->slots, c->graph_slots.data(), sizeof(int) * c->graph_batch, cudaMemcpyHostToDevice), "slots");
+    c->async_slots.clear();
+    ck(cudaMemcpy(c->tokens, tokens, sizeof(int) * c->graph_batch, cudaMemcpyHostToDevice), "tokens");
+  });
+}
+
+int mmc_graph_run(mmc_ctx* c, int32_t n_steps, void* stream) {
+  return guarded([&] {
+    require(c && c->graph, MMC_ERR_STATE, "no graph built");
+    use_device(c);
+    require(n_steps >= 0 && n_steps <= c->hist_cap, MMC_ERR_INVALID, "n_steps outside [0, 8192]");
+    for (int s : c->graph_slots) {
+      require(c->h_pos[s] + n_steps <= int64_t(c->h_pages[s]) * mmc::kPageTokens, MMC_ERR_NO_PAGES,
+              "graph run needs more reserved KV pages (mmc_seq_reserve)");
+      require(c->h_pos[s] + n_steps <= c->d.max_position_embeddings, MMC_ERR_OUT_OF_RANGE,
+              "position exceeds max_position_embeddings");
+    }
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    ck(cudaMemsetAsync(c->hist_step, 0, sizeof(int), st), "history reset");
+    for (int i = 0; i < n_steps; ++i) ck(cudaGraphLaunch(c->graph, st), "graph launch");
+    for (int s : c->graph_slots) c->h_pos[s] += n_steps;
+  });
+}
+
+int mmc_graph_tokens(mmc_ctx* c, int32_t n_steps, int32_t* tokens) {
+  return guarded([&] {
+    require(c && c->graph && tokens, MMC_ERR_STATE, "no graph built");
+    use_device(c);
+    require(n_steps >= 0 && n_steps <= c->hist_cap, MMC_ERR_INVALID, "n_steps out of range");
+    ck(cudaStreamSynchronize(c->stream), "sync");
+    ck(cudaDeviceSynchronize(), "sync");
+    check_device_error(c);
+    ck(cudaMemcpy(tokens, c->hist, sizeof(int) * size_t(n_steps) * c->graph_batch, cudaMemcpyDeviceToHost),
+       "history read");
+  });
+}
+
+int mmc_synchronize(mmc_ctx* c) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    ck(cudaStreamSynchronize(c->stream), "sync");
+    check_device_error(c);
+  });
+}
+
+int mmc_kernels_per_step(const mmc_ctx* c, int32_t, int32_t* k) {
+  return guarded([&] {
+    require(c && k, MMC_ERR_INVALID, "null argument");
+    *k = kernels_per_step(c);
+  });
+}
+
+// ------------------------------------------------------------- single ops
+
+int mmc_op_projection(int32_t batch, int32_t n, int32_t k, const void* w, const float* x, float* y, void* stream) {
+  return guarded([&] {
+    require(batch >= 1 && n > 0 && k > 0 && w && x && y, MMC_ERR_INVALID, "bad projection arguments");
+    require(batch <= 4 ? k % 8 == 0 : k % 64 == 0, MMC_ERR_INVALID, "k must be a multiple of 8 (batch<=4) or 64");
+    mmc::ProjArgs a;
+    a.W = static_cast<const __half*>(w);
+    a.N = n;
+    a.K = k;
+    a.B = batch;
+    a.in = x;
+    a.out = y;
+    a.ldo = n;
+    int dev = 0, sms = 148;
+    ck(cudaGetDevice(&dev), "device");
+    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device query");
+    static thread_local bool attrs = false;
+    if (!attrs) {
+      ck(mmc::gemv_init_attributes(), "attributes");
+      ck(mmc::gemm_init_attributes(), "attributes");
+      attrs = true;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    ck(batch <= 4 ? mmc::launch_gemv(mmc::kProPlain, mmc::kEpiStore, a, sms, s, false)
+                  : mmc::launch_gemm(mmc::kProPlain, mmc::kEpiStore, a, s, false),
+       "projection launch");
+  });
+}
+
+int mmc_op_lm_head_argmax_workspace_size(int32_t batch, int32_t n, int32_t k, size_t* bytes) {
+  return guarded([&] {
+    require(batch >= 1 && n > 0 && k > 0 && bytes, MMC_ERR_INVALID, "bad arguments");
+    int dev = 0, sms = 148;
+    ck(cudaGetDevice(&dev), "device");
+    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device query");
+    const size_t part = batch <= 4 ? mmc::gemv_argmax_part_bytes(n, k, batch, sms) : mmc::gemm_argmax_part_bytes(n, batch);
+    // partials | counters (batch tiles + 2) | token buffer | slots | positions
+    *bytes = (part + 255) / 256 * 256 + 256 * 4 + size_t(batch) * 4 * 3 + 256;
+  });
+}
+
+int mmc_op_lm_head_argmax(int32_t batch, int32_t n, int32_t k, const void* w, const float* x, float* logits,
+                          int32_t* next, void* ws, size_t ws_bytes, void* stream) {
+  return guarded([&] {
+    size_t need = 0;
+    if (mmc_op_lm_head_argmax_workspace_size(batch, n, k, &need) != MMC_OK) fail(MMC_ERR_INVALID, g_error);
+    require(w && x && next && ws && ws_bytes >= need, MMC_ERR_INVALID, "bad arguments or workspace too small");
+    require(batch <= 4 ? k % 8 == 0 : k % 64 == 0, MMC_ERR_INVALID, "k must be a multiple of 8 (batch<=4) or 64");
+    int dev = 0, sms = 148;
+    ck(cudaGetDevice(&dev), "device");
+    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device query");
+    static thread_local bool attrs = false;
+    if (!attrs) {
+      ck(mmc::gemv_init_attributes(), "attributes");
+      ck(mmc::gemm_init_attributes(), "attributes");
+      attrs = true;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t part = batch <= 4 ? mmc::gemv_argmax_part_bytes(n, k, batch, sms) : mmc::gemm_argmax_part_bytes(n, batch);
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    unsigned* counters = reinterpret_cast<unsigned*>(base + (part + 255) / 256 * 256);
+    int* tok = reinterpret_cast<int*>(base + (part + 255) / 256 * 256 + 256 * 4);
+    ck(cudaMemsetAsync(counters, 0, 256 * 4, s), "counter reset");
+    mmc::ProjArgs a;
+    a.W = static_cast<const __half*>(w);
+    a.N = n;
+    a.K = k;
+    a.B = batch;
+    a.in = x;
+    a.logits = logits;
+    a.argmax_part = base;
+    a.counter = counters;
+    a.sink.tokens = tok;
+    a.sink.next_out = next;
+    ck(batch <= 4 ? mmc::launch_gemv(mmc::kProPlain, mmc::kEpiArgmax, a, sms, s, false)
+                  : mmc::launch_gemm(mmc::kProPlain, mmc::kEpiArgmax, a, s, false),
+       "lm_head launch");
+  });
+}
+
+int mmc_op_attention_workspace_size(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t max_ctx,
+                                    size_t* bytes) {
+  return guarded([&] {
+    require(batch >= 1 && nkv >= 1 && nq % nkv == 0 && hd > 0 && max_ctx >= 1 && bytes, MMC_ERR_INVALID,
+            "bad arguments");
+    const int splits = std::min(64, (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens);
+    *bytes = (mmc::attn_part_floats(batch, nkv, splits, nq / nkv, hd) * 4 + 255) / 256 * 256 +
+             size_t(batch) * nkv * 4 + 256;
+  });
+}
+
+int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t layer, int32_t layers,
+                     const float* qkv, const float* q_norm, const float* k_norm, const float* rope_cos,
+                     const float* rope_sin, int32_t max_pos, float eps, void* kv_pool, const int32_t* block_table,
+                     int32_t max_pages, const int32_t* seq_pos, const int32_t* slots, int32_t max_ctx, float* out,
+                     void* ws, size_t ws_bytes, void* stream) {
+  return guarded([&] {
+    size_t need = 0;
+    if (mmc_op_attention_workspace_size(batch, nq, nkv, hd, max_ctx, &need) != MMC_OK) fail(MMC_ERR_INVALID, g_error);
+    require(ws && ws_bytes >= need, MMC_ERR_INVALID, "workspace too small");
+    static thread_local bool attrs = false;
+    if (!attrs) {
+      ck(mmc::attention_init_attributes(), "attributes");
+      attrs = true;
+    }
+    const int pages = (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens;
+    const int splits = std::min(64, pages);
+    const int sp = (pages + splits - 1) / splits;
+    mmc::AttnArgs a;
+    a.qkv = qkv;
+    a.ld_qkv = (nq + 2 * nkv) * hd;
+    a.q_norm = q_norm;
+    a.k_norm = k_norm;
+    a.rope_cos = rope_cos;
+    a.rope_sin = rope_sin;
+    a.max_pos = max_pos;
+    a.eps = eps;
+    a.kv_pool = static_cast<__half*>(kv_pool);
+    a.layer = layer;
+    a.layers = layers;
+    a.block_table = block_table;
+    a.max_pages = max_pages;
+    a.seq_pos = seq_pos;
+    a.slots = slots;
+    a.B = batch;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.hd = hd;
+    a.split_tokens = sp * mmc::kPageTokens;
+    a.max_splits = (pages + sp - 1) / sp;
+    a.out = out;
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    const size_t pbytes = (mmc::attn_part_floats(batch, nkv, splits, nq / nkv, hd) * 4 + 255) / 256 * 256;
+    a.part = reinterpret_cast<float*>(base);
+    a.counters = reinterpret_cast<unsigned*>(base + pbytes);
+    a.err = reinterpret_cast<int*>(base + pbytes + size_t(batch) * nkv * 4);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    ck(cudaMemsetAsync(base + pbytes, 0, size_t(batch) * nkv * 4 + 4, s), "counter reset");
+    ck(mmc::launch_attention(a, s, false), "attention launch");
+  });
+}
+
+int64_t mmc_kv_row_offset(int32_t hd, int32_t row, int32_t chunk) {
+  const int cpr = hd / 8;
+  const int x = (cpr % 8 == 0) ? (row & 7) : ((cpr % 4 == 0) ? ((row >> 1) & 3) : ((row >> 2) & 1));
+  return int64_t(row) * hd + int64_t(chunk ^ x) * 8;
+}
+
+}  // extern "C"

@@ -1,0 +1,186 @@
+"""Per-kernel parity through the C ABI's operator entry points (BASELINE config
+5 shapes): projections, fused lm_head + argmax, fused decode attention. The
+checkers are the CPU oracle's restatements of the reference formulas
+(oracle/minimind_oracle.c) and torch fp32 for the plain projections."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from minimind_orangepi_b200._lib import check, lib
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+SWEEP_SHAPES = [(512, 512), (128, 512), (1408, 512), (512, 1408), (768, 768), (192, 768), (2048, 768),
+                (768, 2048), (6400, 768)]
+
+
+def dev(t):
+    return C.c_void_p(t.data_ptr())
+
+
+@pytest.mark.parametrize("n,k", SWEEP_SHAPES)
+@pytest.mark.parametrize("batch", [1, 3, 8, 64, 256])
+def test_projection(n, k, batch):
+    g = torch.Generator(device="cpu").manual_seed(n * 7 + k + batch)
+    w = (torch.randn(n, k, generator=g) * 0.02).half().cuda()
+    x = torch.randn(batch, k, generator=g).cuda()
+    y = torch.full((batch, n), float("nan"), device="cuda")
+    check(lib().mmc_op_projection(batch, n, k, dev(w), dev(x), dev(y), None))
+    torch.cuda.synchronize()
+    # batches > 4 run on tensor cores with fp16 activations; <= 4 in fp32
+    xr = x if batch <= 4 else x.half().float()
+    ref = xr @ w.float().t()
+    tol = 1e-4 * k ** 0.5 if batch <= 4 else 2e-4 * k ** 0.5
+    assert torch.isfinite(y).all()
+    assert (y - ref).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("batch", [1, 2, 4, 8, 64, 256])
+def test_lm_head_argmax_is_first_max_of_its_own_logits(batch):
+    n, k = 6400, 768
+    g = torch.Generator(device="cpu").manual_seed(batch)
+    w = (torch.randn(n, k, generator=g) * 0.02).half()
+    # plant exact ties: duplicate rows so two vocab ids give the same logit
+    w[4000] = w[17]
+    w[6399] = w[5]
+    w = w.cuda()
+    x = torch.randn(batch, k, generator=g).cuda()
+    logits = torch.empty(batch, n, device="cuda")
+    nxt = torch.full((batch,), -1, dtype=torch.int32, device="cuda")
+    ws_bytes = C.c_size_t()
+    check(lib().mmc_op_lm_head_argmax_workspace_size(batch, n, k, C.byref(ws_bytes)))
+    ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device="cuda")
+    for _ in range(3):  # repeated launches: the arrival counters must self-reset
+        check(lib().mmc_op_lm_head_argmax(batch, n, k, dev(w), dev(x), dev(logits), dev(nxt), dev(ws),
+                                          ws_bytes.value, None))
+    torch.cuda.synchronize()
+    lg = logits.cpu().numpy()
+    got = nxt.cpu().numpy()
+    for b in range(batch):
+        assert got[b] == int(np.argmax(lg[b])), f"row {b}"  # np.argmax = first maximum
+    xr = x if batch <= 4 else x.half().float()
+    ref = (xr @ w.float().t()).cpu().numpy()
+    assert np.abs(lg - ref).max() <= 2e-4 * k ** 0.5
+
+
+def test_lm_head_argmax_tie_goes_to_lowest_index():
+    n, k = 6400, 768
+    w = torch.zeros(n, k, dtype=torch.half)
+    w[:, 0] = 1.0  # every logit equal -> index 0 wins
+    w = w.cuda()
+    for batch in (1, 4, 16):
+        x = torch.ones(batch, k, device="cuda")
+        nxt = torch.full((batch,), -1, dtype=torch.int32, device="cuda")
+        ws_bytes = C.c_size_t()
+        check(lib().mmc_op_lm_head_argmax_workspace_size(batch, n, k, C.byref(ws_bytes)))
+        ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device="cuda")
+        check(lib().mmc_op_lm_head_argmax(batch, n, k, dev(w), dev(x), None, dev(nxt), dev(ws), ws_bytes.value,
+                                          None))
+        torch.cuda.synchronize()
+        assert (nxt.cpu() == 0).all()
+
+
+def _oracle():
+    from oracle.oracle import fptr, lib as olib
+    return olib(), fptr
+
+
+@pytest.mark.parametrize("hd", [64, 96])
+@pytest.mark.parametrize("ctx,batch", [(1, 1), (63, 1), (64, 2), (65, 1), (200, 3), (1024, 2), (8192, 1),
+                                       (32768, 1), (1500, 9)])
+def test_attention_op(hd, ctx, batch):
+    olib, fptr = _oracle()
+    nq, nkv, layers, layer = 8, 2, 2, 1
+    eps, theta = 1e-5, 1e6
+    rng = np.random.default_rng(hd * 1000 + ctx + batch)
+    ctxs = [max(1, ctx - 37 * b) for b in range(batch)]  # ragged rows
+    max_ctx = max(ctxs)
+    half = hd // 2
+    cos_t = np.empty(max_ctx * half, np.float32)
+    sin_t = np.empty(max_ctx * half, np.float32)
+    olib.mmo_rope_tables(max_ctx, hd, theta, fptr(cos_t), fptr(sin_t))
+    qn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    qkv = rng.standard_normal((batch, (nq + 2 * nkv) * hd)).astype(np.float32)
+    max_pages = (max_ctx + 63) // 64
+    n_pages = sum((c + 63) // 64 for c in ctxs) + 1
+    tile = 64 * hd
+    perm = np.array([lib().mmc_kv_row_offset(hd, r, c) for r in range(64) for c in range(hd // 8)])
+    perm = (perm[:, None] + np.arange(8)[None, :]).reshape(-1)  # logical (row, d) -> physical element
+    pool = np.zeros((n_pages, layers, 2, nkv, tile), np.float16)
+    bt = -np.ones((batch, max_pages), np.int32)
+    nxt_page = 1  # page 0 left unused on purpose
+    caches = []
+    for b, c in enumerate(ctxs):
+        pos = c - 1
+        K = (rng.standard_normal((pos, nkv, hd))).astype(np.float16)
+        V = (rng.standard_normal((pos, nkv, hd))).astype(np.float16)
+        caches.append((K, V))
+        for p in range((c + 63) // 64):
+            bt[b, p] = nxt_page
+            nxt_page += 1
+        for p0 in range(0, pos, 64):
+            rows = min(64, pos - p0)
+            for kv, arr in ((0, K), (1, V)):
+                for h in range(nkv):
+                    logical = np.zeros((64, hd), np.float16)
+                    logical[:rows] = arr[p0:p0 + rows, h]
+                    page = pool[bt[b, p0 // 64], layer, kv, h]
+                    page[perm] = logical.reshape(-1)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    d_pool = t(pool)
+    d_bt, d_pos = t(bt), t(np.array([c - 1 for c in ctxs], np.int32))
+    d_slots = t(np.arange(batch, dtype=np.int32))
+    d_qkv, d_qn, d_kn, d_cos, d_sin = t(qkv), t(qn), t(kn), t(cos_t), t(sin_t)
+    out = torch.full((batch, nq * hd), float("nan"), device="cuda")
+    ws_bytes = C.c_size_t()
+    check(lib().mmc_op_attention_workspace_size(batch, nq, nkv, hd, max_ctx, C.byref(ws_bytes)))
+    ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device="cuda")
+    check(lib().mmc_op_attention(batch, nq, nkv, hd, layer, layers, dev(d_qkv), dev(d_qn), dev(d_kn), dev(d_cos),
+                                 dev(d_sin), max_ctx, eps, dev(d_pool), dev(d_bt), max_pages, dev(d_pos),
+                                 dev(d_slots), max_ctx, dev(out), dev(ws), ws_bytes.value, None))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    pool_after = d_pool.cpu().numpy()
+    for b, c in enumerate(ctxs):
+        pos = c - 1
+        row = qkv[b].copy()
+        q = row[:nq * hd].copy()
+        k = row[nq * hd:(nq + nkv) * hd].copy()
+        v = row[(nq + nkv) * hd:].copy()
+        for h in range(nq):
+            seg = q[h * hd:(h + 1) * hd].copy()
+            olib.mmo_rms_norm_inplace(fptr(seg), fptr(qn), hd, eps)
+            q[h * hd:(h + 1) * hd] = seg
+        for h in range(nkv):
+            seg = k[h * hd:(h + 1) * hd].copy()
+            olib.mmo_rms_norm_inplace(fptr(seg), fptr(kn), hd, eps)
+            k[h * hd:(h + 1) * hd] = seg
+        olib.mmo_apply_rope(fptr(q), nq, hd, pos, fptr(cos_t), fptr(sin_t))
+        olib.mmo_apply_rope(fptr(k), nkv, hd, pos, fptr(cos_t), fptr(sin_t))
+        K, V = caches[b]
+        Kf = np.concatenate([K.astype(np.float32), k.reshape(1, nkv, hd)], 0)
+        Vf = np.concatenate([V.astype(np.float32), v.reshape(1, nkv, hd)], 0)
+        ref = np.zeros(nq * hd, np.float32)
+        olib.mmo_attention(fptr(q), fptr(np.ascontiguousarray(Kf)), fptr(np.ascontiguousarray(Vf)), c, nq, nkv, hd,
+                           fptr(ref))
+        err = np.abs(got[b] - ref)
+        assert (err <= 5e-3 + 1e-2 * np.abs(ref)).all(), f"row {b} ctx {c}: max err {err.max():.3e}"
+        # the appended row holds fp16(normed, roped k) and fp16(v)
+        page = bt[b, pos // 64]
+        for kv, vec in ((0, k), (1, v)):
+            for h in range(nkv):
+                phys = pool_after[page, layer, kv, h]
+                logical = np.empty(tile, np.float16)
+                logical[:] = 0
+                logical = phys[perm].reshape(64, hd)[pos % 64]
+                exp = vec[h * hd:(h + 1) * hd].astype(np.float16)
+                assert np.array_equal(logical, exp) or np.abs(logical.astype(np.float32) - exp.astype(
+                    np.float32)).max() <= 1e-3 * np.abs(exp.astype(np.float32)).max()
+    # untouched page 0 stays zero (no stray writes)
+    assert not pool_after[0].any()
