@@ -117,6 +117,12 @@ MMC_EXPORT int mmc_seq_position(const mmc_ctx* ctx, int32_t seq, int64_t* positi
  * ([position][kv_head][head_dim], decoder_layer.h:40-48). */
 MMC_EXPORT int mmc_debug_read_kv(mmc_ctx* ctx, int32_t seq, int32_t layer, float* keys_host, float* values_host);
 
+/* Test helper: copy a per-step scratch buffer of the last step to host fp32:
+ * which = 0 residual stream [batch][hidden], 1 raw q|k|v projections
+ * [batch][(nq + 2 nkv) * hd], 2 attention output [batch][nq * hd],
+ * 3 SiLU*mul activations [batch][intermediate]. `count` floats are copied. */
+MMC_EXPORT int mmc_debug_scratch(mmc_ctx* ctx, int32_t which, float* host, int64_t count);
+
 /* ------------------------------------------------------------- decode */
 
 /* One greedy decode step for `batch` sequences — the batched form of

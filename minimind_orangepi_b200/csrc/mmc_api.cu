@@ -140,6 +140,14 @@ namespace {
 
 void use_device(const mmc_ctx* c) { ck(cudaSetDevice(c->device), "cudaSetDevice"); }
 
+// Host -> device copy ordered on the context's stream and complete on return.
+// (A plain cudaMemcpy from pageable memory may return before its DMA lands and
+// is not ordered with work on the context's non-blocking stream.)
+void upload(const mmc_ctx* c, void* dst, const void* src, size_t bytes, const char* what) {
+  ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->stream), what);
+  ck(cudaStreamSynchronize(c->stream), what);
+}
+
 void require(bool ok, int code, const std::string& msg) {
   if (!ok) fail(code, msg);
 }
@@ -148,7 +156,8 @@ void check_device_error(mmc_ctx* c) {
   int e = 0;
   ck(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
   if (e != 0) {
-    ck(cudaMemset(c->err, 0, sizeof(int)), "clear device error word");
+    ck(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream), "clear device error word");
+    ck(cudaStreamSynchronize(c->stream), "clear device error word");
     const char* what = e == mmc::kDevWaitTimeout   ? "a bounded wait timed out"
                        : e == mmc::kDevBadToken    ? "token id out of vocabulary range"
                        : e == mmc::kDevNoPage      ? "KV position not backed by a reserved page"
@@ -327,10 +336,8 @@ void reserve_pages(mmc_ctx* c, int32_t seq, int64_t tokens) {
   }
   const int old = c->h_pages[seq];
   c->h_pages[seq] = need;
-  ck(cudaMemcpy(c->d_block_table + size_t(seq) * c->max_pages + old,
-                c->h_block_table.data() + size_t(seq) * c->max_pages + old, sizeof(int) * (need - old),
-                cudaMemcpyHostToDevice),
-     "block table upload");
+  upload(c, c->d_block_table + size_t(seq) * c->max_pages + old,
+         c->h_block_table.data() + size_t(seq) * c->max_pages + old, sizeof(int) * (need - old), "block table upload");
 }
 
 // Host-side checks shared by the eager step entry points; returns the plan.
@@ -415,7 +422,7 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
   std::vector<float> host, host2;
   auto put = [&](int i, float* dst_d) {
     get(i, host);
-    ck(cudaMemcpy(dst_d, host.data(), host.size() * 4, cudaMemcpyHostToDevice), "weight upload");
+    upload(c, dst_d, host.data(), host.size() * 4, "weight upload");
   };
   c->embed = c->alloc<float>(size_t(V * H), "embed");
   put(0, c->embed);
@@ -466,8 +473,9 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
   const auto sin_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, true);
   c->rope_cos = c->alloc<float>(cos_t.size(), "rope");
   c->rope_sin = c->alloc<float>(sin_t.size(), "rope");
-  ck(cudaMemcpy(c->rope_cos, cos_t.data(), cos_t.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-  ck(cudaMemcpy(c->rope_sin, sin_t.data(), sin_t.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+  upload(c, c->rope_cos, cos_t.data(), cos_t.size() * 4, "rope upload");
+  upload(c, c->rope_sin, sin_t.data(), sin_t.size() * 4, "rope upload");
+  ck(cudaDeviceSynchronize(), "weight upload");
   c->loaded = true;
 }
 
@@ -516,6 +524,7 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     ck(mmc::gemm_init_attributes(), "gemm attributes");
     ck(mmc::attention_init_attributes(), "attention attributes");
     c->err = c->alloc<int>(1, "error word");
+    ck(cudaDeviceSynchronize(), "context init");
     *out = c.release();
   });
 }
@@ -599,8 +608,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->d_block_table = c->alloc<int>(size_t(max_seqs) * c->max_pages, "block table");
     c->d_seq_pos = c->alloc<int>(size_t(max_seqs), "positions");
     c->h_block_table.assign(size_t(max_seqs) * c->max_pages, -1);
-    ck(cudaMemcpy(c->d_block_table, c->h_block_table.data(), c->h_block_table.size() * 4, cudaMemcpyHostToDevice),
-       "block table init");
+    upload(c, c->d_block_table, c->h_block_table.data(), c->h_block_table.size() * 4, "block table init");
     c->h_pos.assign(size_t(max_seqs), 0);
     c->h_pages.assign(size_t(max_seqs), 0);
     c->h_open.assign(size_t(max_seqs), 0);
@@ -627,6 +635,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
         "attention partials");
     c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
     ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
+    ck(cudaDeviceSynchronize(), "KV init");
     c->kv_ready = true;
   });
 }
@@ -647,7 +656,7 @@ int mmc_seq_open(mmc_ctx* c, int64_t reserve_tokens, int32_t* seq_out) {
     c->h_pos[s] = 0;
     c->h_pages[s] = 0;
     const int zero = 0;
-    ck(cudaMemcpy(c->d_seq_pos + s, &zero, sizeof(int), cudaMemcpyHostToDevice), "position reset");
+    upload(c, c->d_seq_pos + s, &zero, sizeof(int), "position reset");
     try {
       reserve_pages(c, s, std::max<int64_t>(reserve_tokens, 1));
     } catch (...) {
@@ -679,10 +688,8 @@ int mmc_seq_close(mmc_ctx* c, int32_t seq) {
       e = -1;
     }
     if (c->h_pages[seq] > 0)
-      ck(cudaMemcpy(c->d_block_table + size_t(seq) * c->max_pages,
-                    c->h_block_table.data() + size_t(seq) * c->max_pages, sizeof(int) * c->h_pages[seq],
-                    cudaMemcpyHostToDevice),
-         "block table upload");
+      upload(c, c->d_block_table + size_t(seq) * c->max_pages, c->h_block_table.data() + size_t(seq) * c->max_pages,
+             sizeof(int) * c->h_pages[seq], "block table upload");
     c->h_pages[seq] = 0;
     c->h_open[seq] = 0;
     c->h_pos[seq] = 0;
@@ -725,6 +732,21 @@ int mmc_debug_read_kv(mmc_ctx* c, int32_t seq, int32_t layer, float* keys, float
               }
         }
     }
+  });
+}
+
+int mmc_debug_scratch(mmc_ctx* c, int32_t which, float* host, int64_t count) {
+  return guarded([&] {
+    require(c && host && count >= 0, MMC_ERR_INVALID, "null argument");
+    require_ready(c);
+    use_device(c);
+    const float* src = which == 0 ? c->hidden : which == 1 ? c->qkv : which == 2 ? c->attn : which == 3 ? c->act : nullptr;
+    require(src != nullptr, MMC_ERR_INVALID, "unknown scratch buffer");
+    const int64_t cap = int64_t(c->max_batch) * (which == 0 ? c->d.hidden_size : which == 1 ? c->q_size() + 2 * c->kv_size()
+                                                  : which == 2 ? c->q_size() : c->d.intermediate_size);
+    require(count <= cap, MMC_ERR_INVALID, "count exceeds the buffer");
+    ck(cudaStreamSynchronize(c->stream), "sync");
+    ck(cudaMemcpy(host, src, size_t(count) * 4, cudaMemcpyDeviceToHost), "scratch read");
   });
 }
 
@@ -772,7 +794,7 @@ int mmc_decode_step_async(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, con
     if (c->async_slots.size() != size_t(batch) || !std::equal(seq_ids, seq_ids + batch, c->async_slots.begin())) {
       // the slot list changes rarely: upload it synchronously and remember it
       ck(cudaStreamSynchronize(s), "drain before slot upload");
-      ck(cudaMemcpy(c->slots, seq_ids, sizeof(int) * batch, cudaMemcpyHostToDevice), "H2D slots");
+      upload(c, c->slots, seq_ids, sizeof(int) * batch, "H2D slots");
       c->async_slots.assign(seq_ids, seq_ids + batch);
     }
     ck(cudaMemcpyAsync(c->tokens, d_tokens, sizeof(int) * batch, cudaMemcpyDeviceToDevice, s), "tokens");
@@ -809,7 +831,7 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
       c->hist = c->alloc<int>(size_t(c->hist_cap) * c->max_batch, "token history");
       c->hist_step = c->alloc<int>(1, "history counter");
     }
-    ck(cudaMemcpy(c->slots, seq_ids, sizeof(int) * batch, cudaMemcpyHostToDevice), "slots");
+    upload(c, c->slots, seq_ids, sizeof(int) * batch, "slots");
     c->async_slots.clear();
     io.slots = c->slots;
     io.tokens = c->tokens;
@@ -840,9 +862,9 @@ int mmc_graph_set_tokens(mmc_ctx* c, const int32_t* tokens) {
     use_device(c);
     for (int b = 0; b < c->graph_batch; ++b)
       require(tokens[b] >= 0 && tokens[b] < c->d.vocab_size, MMC_ERR_OUT_OF_RANGE, "token id out of vocabulary range");
-    ck(cudaMemcpy(c->slots, c->graph_slots.data(), sizeof(int) * c->graph_batch, cudaMemcpyHostToDevice), "slots");
+    upload(c, c->slots, c->graph_slots.data(), sizeof(int) * c->graph_batch, "slots");
     c->async_slots.clear();
-    ck(cudaMemcpy(c->tokens, tokens, sizeof(int) * c->graph_batch, cudaMemcpyHostToDevice), "tokens");
+    upload(c, c->tokens, tokens, sizeof(int) * c->graph_batch, "tokens");
   });
 }
 
