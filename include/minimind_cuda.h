@@ -130,11 +130,22 @@ MMC_EXPORT int mmc_debug_scratch(mmc_ctx* ctx, int32_t which, float* host, int64
  * embedding -> layers -> final norm -> lm_head -> argmax (first maximum).
  * Host buffers; synchronous. `logits_host` (optional, [batch][vocab]) receives
  * the fp32 logits like LanguageModel::forward_token (language_model.cpp:297-308).
- * Each sequence's position advances by one. A token outside the vocabulary
+ * Each sequence's position advances by one. When a graph was built for
+ * exactly this list of sequences (mmc_graph_build) and no logits are asked
+ * for, the step replays that graph instead of launching kernel by kernel.
+ * A token outside the vocabulary
  * fails with MMC_ERR_OUT_OF_RANGE before anything runs (embedding_row,
  * language_model.cpp:67-77). */
 MMC_EXPORT int mmc_decode_step(mmc_ctx* ctx, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
                     int32_t* next_tokens, float* logits_host);
+
+/* One decode step like mmc_decode_step, with a CUDA event between every two
+ * kernels (programmatic overlap off) so each kernel's device time is
+ * measured. kind_ms[6] / kind_launches[6] receive the summed milliseconds and
+ * launch counts per kernel kind: 0 qkv projection, 1 attention, 2 o
+ * projection, 3 gate/up projection, 4 down projection, 5 lm_head + argmax. */
+MMC_EXPORT int mmc_profile_step(mmc_ctx* ctx, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
+                                int32_t* next_tokens, float* kind_ms, int32_t* kind_launches);
 
 /* Same step, asynchronous on `stream`, with the tokens in device memory
  * (`d_tokens` read, `d_next` written, `d_logits` optional). Sequence ids are
@@ -155,7 +166,8 @@ MMC_EXPORT int mmc_graph_tokens(mmc_ctx* ctx, int32_t n_steps, int32_t* tokens_h
 
 /* Wait for the context's stream and report any device-side error. */
 MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
-/* Number of kernels one decode step launches for a batch of `batch` rows. */
+/* Number of kernels one decode step launches for a batch of `batch` rows
+ * (5 per layer + 1 for batch <= 4, 7 per layer + 2 above). */
 MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* kernels);
 
 /* ------------------------------------------------------------- single ops
@@ -164,14 +176,17 @@ MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* 
  * workspace): used by the per-kernel parity tests and the kernel sweep. All
  * pointers are device pointers; launches are asynchronous on `stream`. */
 
-/* y[b][n] = sum_k W[n][k] x[b][k]; W fp16 [N][K] row-major, x/y fp32.
- * Replaces device_matmul (ascend_matmul.cpp:385-410). No workspace. */
-MMC_EXPORT int mmc_op_projection(int32_t batch, int32_t n, int32_t k, const void* d_w_fp16, const float* d_x, float* d_y,
+/* y[b][n] = sum_k W[n][k] x[b][k]; W fp16 [N][K] row-major, y fp32.
+ * x is fp32 [batch][k] when batch <= 4 (CUDA-core path) and fp16 when
+ * batch > 4 (tcgen05 tensor-core path). Replaces device_matmul
+ * (ascend_matmul.cpp:385-410). No workspace. */
+MMC_EXPORT int mmc_op_projection(int32_t batch, int32_t n, int32_t k, const void* d_w_fp16, const void* d_x, float* d_y,
                       void* stream);
 /* Fused lm_head GEMV + argmax: logits (optional) and the first-maximum index
- * per row. Replaces device_matmul_argmax (ascend_matmul.cpp:467-497). */
+ * per row (x typed as for mmc_op_projection). Replaces device_matmul_argmax
+ * (ascend_matmul.cpp:467-497). */
 MMC_EXPORT int mmc_op_lm_head_argmax_workspace_size(int32_t batch, int32_t n, int32_t k, size_t* bytes);
-MMC_EXPORT int mmc_op_lm_head_argmax(int32_t batch, int32_t n, int32_t k, const void* d_w_fp16, const float* d_x,
+MMC_EXPORT int mmc_op_lm_head_argmax(int32_t batch, int32_t n, int32_t k, const void* d_w_fp16, const void* d_x,
                           float* d_logits, int32_t* d_next, void* d_workspace, size_t workspace_bytes, void* stream);
 /* Fused q/k RMSNorm + RoPE + K/V append + GQA decode attention for one layer
  * over a paged cache. Replaces device_decode_qkv_postprocess +

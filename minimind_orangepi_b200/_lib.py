@@ -53,6 +53,8 @@ EXPORTS = {
     "mmc_debug_read_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     "mmc_debug_scratch": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int64]),
     "mmc_decode_step": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "mmc_profile_step": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p]),
     "mmc_decode_step_async": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p]),
     "mmc_graph_build": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p]),

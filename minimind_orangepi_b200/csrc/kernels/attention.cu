@@ -304,7 +304,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
 
   const size_t pstride = (size_t)rep * (HD + 2);
   float* part_bh = a.part + ((size_t)b * a.nkv + h) * a.max_splits * pstride;
-  float* out_bh = a.out + (size_t)b * a.nq * HD + (size_t)h * rep * HD;
+  const size_t out_off = (size_t)b * a.nq * HD + (size_t)h * rep * HD;
+  auto put_out = [&](int idx, float v) {
+    if (a.out16) a.out16[out_off + idx] = __float2half_rn(v);
+    else a.out[out_off + idx] = v;
+  };
   for (int i = tid; i < rep * HD; i += kAttnThreads) {
     const int j = i / HD, d = i % HD;
     float M = -1e30f;
@@ -317,7 +321,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
       O += cw[d] * f;
     }
     if (nsplits == 1) {
-      out_bh[j * HD + d] = O / L;
+      put_out(j * HD + d, O / L);
     } else {
       float* p = part_bh + split * pstride + j * (HD + 2);
       p[d] = O;
@@ -347,7 +351,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
       L += __ldcg(p + HD + 1) * f;
       O += __ldcg(p + d) * f;
     }
-    out_bh[j * HD + d] = O / L;
+    put_out(j * HD + d, O / L);
   }
   if (tid == 0) a.counters[(size_t)b * a.nkv + h] = 0u;
 }

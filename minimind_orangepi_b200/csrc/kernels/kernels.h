@@ -77,11 +77,41 @@ size_t gemv_argmax_part_bytes(int N, int K, int B, int num_sms);
 cudaError_t launch_gemv(int pro, int epi, const ProjArgs& a, int num_sms, cudaStream_t stream, bool pdl);
 cudaError_t gemv_init_attributes();
 
-// Tensor-core projection for batches B > 4 (mma.sync m16n8k16, fp16 inputs,
-// fp32 accumulate): weights on the M side, batch on N.
-size_t gemm_argmax_part_bytes(int N, int B);
-cudaError_t launch_gemm(int pro, int epi, const ProjArgs& a, cudaStream_t stream, bool pdl);
-cudaError_t gemm_init_attributes();
+// Tensor-core projection for batches B > 4 (tcgen05.mma, fp16 operands, fp32
+// accumulate in TMEM): weight rows on the UMMA M side, batch rows on N.
+struct TcArgs {
+  const __half* W = nullptr;  // [N][K] fp16
+  const __half* X = nullptr;  // [B][K] fp16 activations
+  int N = 0, K = 0, B = 0;
+  float* out = nullptr;     // kEpiStore / kEpiResid: [B][ldo] fp32
+  __half* out16 = nullptr;  // kEpiSwiglu: [B][ldo] fp16
+  int ldo = 0;
+  float* logits = nullptr;       // kEpiArgmax: optional [B][N]
+  void* argmax_part = nullptr;   // kEpiArgmax: [B][ceil(N/128)] (value, index)
+  unsigned* counter = nullptr;   // kEpiArgmax: tc_counter_words zeroed words
+  TokenSink sink;
+  int* err = nullptr;
+};
+int tc_batch_tile(int N, int B);
+size_t tc_argmax_part_bytes(int N, int B);
+int tc_counter_words(int N, int B);
+cudaError_t launch_gemm_tc(int epi, const TcArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t gemm_tc_init_attributes();
+
+// RMSNorm of B rows to fp16 (input of the tensor-core projections).
+struct NormArgs {
+  const float* hidden = nullptr;  // [B][H] residual stream (written from embed when embedding)
+  float* hidden_out = nullptr;
+  const float* w = nullptr;
+  float eps = 0.f;
+  __half* out = nullptr;  // [B][H]
+  int B = 0, H = 0;
+  const float* embed = nullptr;
+  const int* tokens = nullptr;
+  int vocab = 0;
+  int* err = nullptr;
+};
+cudaError_t launch_rmsnorm_f16(const NormArgs& a, bool embed, bool final_norm, cudaStream_t stream, bool pdl);
 
 // Fused decode attention: q/k per-head RMSNorm + rotate-half RoPE, K/V append
 // into the paged cache, split-KV GQA flash-decode over the cache, split
@@ -104,7 +134,8 @@ struct AttnArgs {
   int B = 0, nq = 0, nkv = 0, hd = 0;
   int split_tokens = 0;  // multiple of the page size
   int max_splits = 0;    // grid.x
-  float* out = nullptr;  // [B][nq * hd] fp32
+  float* out = nullptr;     // [B][nq * hd] fp32, or
+  __half* out16 = nullptr;  // [B][nq * hd] fp16 when set (tensor-core path)
   float* part = nullptr;  // [B][nkv][max_splits][rep][hd + 2] split partials
   unsigned* counters = nullptr;  // [B][nkv], zero-initialised, self-resetting
   int* err = nullptr;

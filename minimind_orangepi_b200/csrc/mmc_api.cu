@@ -107,6 +107,7 @@ struct mmc_ctx {
 
   // per-step scratch (sized for max_batch)
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+  __half *xn16 = nullptr, *attn16 = nullptr, *act16 = nullptr;  // tensor-core path activations
   int *tokens = nullptr, *slots = nullptr, *next = nullptr;
   void* argmax_part = nullptr;
   unsigned* argmax_counter = nullptr;
@@ -124,6 +125,7 @@ struct mmc_ctx {
   int* hist = nullptr;
   int* hist_step = nullptr;
   int hist_cap = 0;
+  int64_t graph_cap_tokens = 0;  // positions the captured split plan covers
 
   template <typename T>
   T* alloc(size_t n, const char* what) {
@@ -137,6 +139,8 @@ struct mmc_ctx {
 };
 
 namespace {
+
+constexpr int mmc_kernel_kinds = 7;
 
 void use_device(const mmc_ctx* c) { ck(cudaSetDevice(c->device), "cudaSetDevice"); }
 
@@ -191,41 +195,99 @@ struct StepIO {
   int max_splits = 1;
 };
 
-int kernels_per_step(const mmc_ctx* c) { return int(c->d.num_hidden_layers) * 5 + 1; }
+// Batches of up to kGemvMaxBatch rows use the CUDA-core projections with
+// fused RMSNorm prologues (5 kernels per layer); larger batches the tensor-core
+// projections behind an fp16 RMSNorm kernel (7 per layer).
+constexpr int kGemvMaxBatch = 4;
+enum Kind { kKindQkv = 0, kKindAttn = 1, kKindO = 2, kKindGateUp = 3, kKindDown = 4, kKindLm = 5, kKindNorm = 6 };
 
-void launch_proj(mmc_ctx* c, int pro, int epi, const mmc::ProjArgs& a, cudaStream_t s, bool pdl) {
-  cudaError_t e = a.B <= 4 ? mmc::launch_gemv(pro, epi, a, c->num_sms, s, pdl) : mmc::launch_gemm(pro, epi, a, s, pdl);
-  ck(e, "projection launch");
+int kernels_per_step(const mmc_ctx* c, int B) {
+  const int L = int(c->d.num_hidden_layers);
+  return B <= kGemvMaxBatch ? 5 * L + 1 : 7 * L + 2;
 }
 
-void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
+void launch_proj(mmc_ctx* c, int pro, int epi, const mmc::ProjArgs& a, cudaStream_t s, bool pdl) {
+  ck(mmc::launch_gemv(pro, epi, a, c->num_sms, s, pdl), "projection launch");
+}
+
+// `ev` (optional, kernels_per_step + 1 events): recorded before every launch
+// and after the last one, with programmatic overlap disabled, so the gaps are
+// per-kernel device durations; `kinds` receives each launch's Kind.
+void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev = nullptr,
+                  std::vector<int>* kinds = nullptr) {
   const auto& d = c->d;
   const int H = int(d.hidden_size), I = int(d.intermediate_size), Q = c->q_size(), KV = c->kv_size();
   const int NQKV = Q + 2 * KV;
-  bool pdl = false;
+  const bool tc = io.B > kGemvMaxBatch;
+  int evi = 0;
+  bool first = true;
+  // returns whether this launch may use programmatic overlap
+  auto mark = [&](Kind k) {
+    if (ev) ck(cudaEventRecord(ev[evi++], s), "event record");
+    if (kinds) kinds->push_back(k);
+    const bool pdl = !first && ev == nullptr;
+    first = false;
+    return pdl;
+  };
+  auto norm16 = [&](const float* w, bool embed, bool final_norm) {
+    mmc::NormArgs n;
+    n.hidden = c->hidden;
+    n.hidden_out = c->hidden;
+    n.w = w;
+    n.eps = d.rms_norm_eps;
+    n.out = c->xn16;
+    n.B = io.B;
+    n.H = H;
+    n.embed = c->embed;
+    n.tokens = io.tokens;
+    n.vocab = int(d.vocab_size);
+    n.err = c->err;
+    const bool pdl = mark(kKindNorm);
+    ck(mmc::launch_rmsnorm_f16(n, embed, final_norm, s, pdl), "rmsnorm launch");
+  };
+  auto tcproj = [&](Kind k, int epi, const __half* W, int N, int K, const __half* X, float* out, __half* out16,
+                    int ldo) {
+    mmc::TcArgs t;
+    t.W = W;
+    t.X = X;
+    t.N = N;
+    t.K = K;
+    t.B = io.B;
+    t.out = out;
+    t.out16 = out16;
+    t.ldo = ldo;
+    t.err = c->err;
+    const bool pdl = mark(k);
+    ck(mmc::launch_gemm_tc(epi, t, s, pdl), "tensor-core projection launch");
+  };
   for (int l = 0; l < int(d.num_hidden_layers); ++l) {
     const Layer& L = c->layers[l];
-    mmc::ProjArgs p;
-    p.B = io.B;
-    p.err = c->err;
-    // qkv
-    p.W = L.qkv;
-    p.N = NQKV;
-    p.K = H;
-    p.in = c->hidden;
-    p.norm_w = L.in_norm;
-    p.eps = d.rms_norm_eps;
-    p.out = c->qkv;
-    p.ldo = NQKV;
-    if (l == 0) {
-      p.embed = c->embed;
-      p.vocab = int(d.vocab_size);
-      p.tokens = io.tokens;
-      p.hidden = c->hidden;
+    // ---- q|k|v projection
+    if (tc) {
+      norm16(L.in_norm, l == 0, false);
+      tcproj(kKindQkv, mmc::kEpiStore, L.qkv, NQKV, H, c->xn16, c->qkv, nullptr, NQKV);
+    } else {
+      mmc::ProjArgs p;
+      p.B = io.B;
+      p.err = c->err;
+      p.W = L.qkv;
+      p.N = NQKV;
+      p.K = H;
+      p.in = c->hidden;
+      p.norm_w = L.in_norm;
+      p.eps = d.rms_norm_eps;
+      p.out = c->qkv;
+      p.ldo = NQKV;
+      if (l == 0) {
+        p.embed = c->embed;
+        p.vocab = int(d.vocab_size);
+        p.tokens = io.tokens;
+        p.hidden = c->hidden;
+      }
+      const bool pdl = mark(kKindQkv);
+      launch_proj(c, l == 0 ? mmc::kProEmbedNorm : mmc::kProNorm, mmc::kEpiStore, p, s, pdl);
     }
-    launch_proj(c, l == 0 ? mmc::kProEmbedNorm : mmc::kProNorm, mmc::kEpiStore, p, s, pdl);
-    pdl = true;
-    // attention
+    // ---- attention
     mmc::AttnArgs a;
     a.qkv = c->qkv;
     a.ld_qkv = NQKV;
@@ -248,12 +310,23 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
     a.hd = int(d.head_dim);
     a.split_tokens = io.split_tokens;
     a.max_splits = io.max_splits;
-    a.out = c->attn;
+    a.out = tc ? nullptr : c->attn;
+    a.out16 = tc ? c->attn16 : nullptr;
     a.part = c->attn_part;
     a.counters = c->attn_counters;
     a.err = c->err;
-    ck(mmc::launch_attention(a, s, pdl), "attention launch");
-    // o projection + residual
+    {
+      const bool pdl = mark(kKindAttn);
+      ck(mmc::launch_attention(a, s, pdl), "attention launch");
+    }
+    if (tc) {
+      tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, c->attn16, c->hidden, nullptr, H);
+      norm16(L.post_norm, false, false);
+      tcproj(kKindGateUp, mmc::kEpiSwiglu, L.gu, 2 * I, H, c->xn16, nullptr, c->act16, I);
+      tcproj(kKindDown, mmc::kEpiResid, L.down, H, I, c->act16, c->hidden, nullptr, H);
+      continue;
+    }
+    // ---- o projection + residual
     mmc::ProjArgs o;
     o.B = io.B;
     o.err = c->err;
@@ -263,8 +336,11 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
     o.in = c->attn;
     o.out = c->hidden;
     o.ldo = H;
-    launch_proj(c, mmc::kProPlain, mmc::kEpiResid, o, s, pdl);
-    // gate/up + SiLU*mul
+    {
+      const bool pdl = mark(kKindO);
+      launch_proj(c, mmc::kProPlain, mmc::kEpiResid, o, s, pdl);
+    }
+    // ---- gate/up + SiLU*mul
     mmc::ProjArgs gu;
     gu.B = io.B;
     gu.err = c->err;
@@ -276,8 +352,11 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
     gu.eps = d.rms_norm_eps;
     gu.out = c->act;
     gu.ldo = I;
-    launch_proj(c, mmc::kProNorm, mmc::kEpiSwiglu, gu, s, pdl);
-    // down + residual
+    {
+      const bool pdl = mark(kKindGateUp);
+      launch_proj(c, mmc::kProNorm, mmc::kEpiSwiglu, gu, s, pdl);
+    }
+    // ---- down + residual
     mmc::ProjArgs dn;
     dn.B = io.B;
     dn.err = c->err;
@@ -287,29 +366,53 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
     dn.in = c->act;
     dn.out = c->hidden;
     dn.ldo = H;
-    launch_proj(c, mmc::kProPlain, mmc::kEpiResid, dn, s, pdl);
+    {
+      const bool pdl = mark(kKindDown);
+      launch_proj(c, mmc::kProPlain, mmc::kEpiResid, dn, s, pdl);
+    }
   }
-  // final norm + lm_head + argmax
-  mmc::ProjArgs lm;
-  lm.B = io.B;
-  lm.err = c->err;
-  lm.W = c->lm_head;
-  lm.N = int(d.vocab_size);
-  lm.K = H;
-  lm.in = c->hidden;
-  lm.norm_w = c->final_norm;
-  lm.eps = d.rms_norm_eps;
-  lm.logits = io.logits;
-  lm.argmax_part = c->argmax_part;
-  lm.counter = c->argmax_counter;
-  lm.sink.tokens = io.tokens;
-  lm.sink.next_out = io.next_out;
-  lm.sink.seq_pos = c->d_seq_pos;
-  lm.sink.slots = io.slots;
-  lm.sink.hist = io.hist;
-  lm.sink.hist_step = io.hist_step;
-  lm.sink.hist_cap = io.hist_cap;
-  launch_proj(c, mmc::kProNormFinal, mmc::kEpiArgmax, lm, s, true);
+  // ---- final norm + lm_head + argmax (next tokens, positions, history)
+  mmc::TokenSink sink;
+  sink.tokens = io.tokens;
+  sink.next_out = io.next_out;
+  sink.seq_pos = c->d_seq_pos;
+  sink.slots = io.slots;
+  sink.hist = io.hist;
+  sink.hist_step = io.hist_step;
+  sink.hist_cap = io.hist_cap;
+  if (tc) {
+    norm16(c->final_norm, false, true);
+    mmc::TcArgs t;
+    t.W = c->lm_head;
+    t.X = c->xn16;
+    t.N = int(d.vocab_size);
+    t.K = H;
+    t.B = io.B;
+    t.logits = io.logits;
+    t.argmax_part = c->argmax_part;
+    t.counter = c->argmax_counter;
+    t.sink = sink;
+    t.err = c->err;
+    const bool pdl = mark(kKindLm);
+    ck(mmc::launch_gemm_tc(mmc::kEpiArgmax, t, s, pdl), "lm_head launch");
+  } else {
+    mmc::ProjArgs lm;
+    lm.B = io.B;
+    lm.err = c->err;
+    lm.W = c->lm_head;
+    lm.N = int(d.vocab_size);
+    lm.K = H;
+    lm.in = c->hidden;
+    lm.norm_w = c->final_norm;
+    lm.eps = d.rms_norm_eps;
+    lm.logits = io.logits;
+    lm.argmax_part = c->argmax_part;
+    lm.counter = c->argmax_counter;
+    lm.sink = sink;
+    const bool pdl = mark(kKindLm);
+    launch_proj(c, mmc::kProNormFinal, mmc::kEpiArgmax, lm, s, pdl);
+  }
+  if (ev) ck(cudaEventRecord(ev[evi++], s), "event record");
 }
 
 void require_ready(const mmc_ctx* c) {
@@ -521,7 +624,7 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     ck(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device), "device query");
     ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
     ck(mmc::gemv_init_attributes(), "gemv attributes");
-    ck(mmc::gemm_init_attributes(), "gemm attributes");
+    ck(mmc::gemm_tc_init_attributes(), "tensor-core projection attributes");
     ck(mmc::attention_init_attributes(), "attention attributes");
     c->err = c->alloc<int>(1, "error word");
     ck(cudaDeviceSynchronize(), "context init");
@@ -620,6 +723,9 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->qkv = c->alloc<float>(size_t(max_batch) * (Q + 2 * KV), "qkv");
     c->attn = c->alloc<float>(size_t(max_batch) * Q, "attn");
     c->act = c->alloc<float>(size_t(max_batch) * I, "act");
+    c->xn16 = c->alloc<__half>(size_t(max_batch) * H, "normed activations");
+    c->attn16 = c->alloc<__half>(size_t(max_batch) * Q, "attention output fp16");
+    c->act16 = c->alloc<__half>(size_t(max_batch) * I, "act fp16");
     c->logits = c->alloc<float>(size_t(max_batch) * V, "logits");
     c->tokens = c->alloc<int>(size_t(max_batch), "tokens");
     c->slots = c->alloc<int>(size_t(max_batch), "slots");
@@ -627,7 +733,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     size_t part_bytes = 0;
     for (int b = 1; b <= std::min(max_batch, 4); ++b)
       part_bytes = std::max(part_bytes, mmc::gemv_argmax_part_bytes(V, H, b, c->num_sms));
-    part_bytes = std::max(part_bytes, mmc::gemm_argmax_part_bytes(V, max_batch));
+    part_bytes = std::max(part_bytes, mmc::tc_argmax_part_bytes(V, max_batch));
     c->argmax_part = c->alloc<uint8_t>(part_bytes, "argmax partials");
     c->argmax_counter = c->alloc<unsigned>(size_t(max_batch) + 2, "argmax counters");
     c->attn_part = c->alloc<float>(
@@ -766,10 +872,18 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     c->async_slots.clear();
     ck(cudaMemcpyAsync(c->tokens, c->h_stage + batch, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream),
        "H2D tokens");
+    const bool use_graph = c->graph && !logits_host && batch == c->graph_batch &&
+                           std::equal(seq_ids, seq_ids + batch, c->graph_slots.begin()) &&
+                           std::all_of(seq_ids, seq_ids + batch,
+                                       [&](int32_t q) { return c->h_pos[q] + 1 <= c->graph_cap_tokens; });
     io.slots = c->slots;
     io.tokens = c->tokens;
     io.logits = logits_host ? c->logits : nullptr;
-    enqueue_step(c, io, c->stream);
+    if (use_graph) {
+      ck(cudaGraphLaunch(c->graph, c->stream), "graph launch");
+    } else {
+      enqueue_step(c, io, c->stream);
+    }
     ck(cudaMemcpyAsync(c->h_stage + 2 * batch, c->tokens, sizeof(int) * batch, cudaMemcpyDeviceToHost, c->stream),
        "D2H next tokens");
     if (logits_host)
@@ -779,6 +893,50 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     ck(cudaStreamSynchronize(c->stream), "decode step");
     check_device_error(c);
     std::memcpy(next_tokens, c->h_stage + 2 * batch, sizeof(int) * batch);
+    for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
+  });
+}
+
+int mmc_profile_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int32_t* tokens, int32_t* next_tokens,
+                     float* kind_ms, int32_t* kind_launches) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    require(tokens && next_tokens && kind_ms && kind_launches, MMC_ERR_INVALID, "null argument");
+    StepIO io = plan_step(c, batch, seq_ids, /*auto_reserve=*/true);
+    for (int b = 0; b < batch; ++b)
+      require(tokens[b] >= 0 && tokens[b] < c->d.vocab_size, MMC_ERR_OUT_OF_RANGE,
+              "token id out of vocabulary range");
+    upload(c, c->slots, seq_ids, sizeof(int) * batch, "H2D slots");
+    upload(c, c->tokens, tokens, sizeof(int) * batch, "H2D tokens");
+    c->async_slots.clear();
+    io.slots = c->slots;
+    io.tokens = c->tokens;
+    const int n = kernels_per_step(c, batch);
+    std::vector<cudaEvent_t> ev(size_t(n) + 1);
+    std::vector<int> kinds;
+    for (auto& e : ev) ck(cudaEventCreate(&e), "event create");
+    try {
+      enqueue_step(c, io, c->stream, ev.data(), &kinds);
+      ck(cudaStreamSynchronize(c->stream), "profiled step");
+      check_device_error(c);
+      for (int k = 0; k < mmc_kernel_kinds; ++k) {
+        kind_ms[k] = 0.f;
+        kind_launches[k] = 0;
+      }
+      for (int i = 0; i < n; ++i) {
+        float ms = 0.f;
+        ck(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "event time");
+        const int kind = kinds[size_t(i)];
+        kind_ms[kind] += ms;
+        kind_launches[kind] += 1;
+      }
+    } catch (...) {
+      for (auto& e : ev) cudaEventDestroy(e);
+      throw;
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    ck(cudaMemcpy(next_tokens, c->tokens, sizeof(int) * batch, cudaMemcpyDeviceToHost), "D2H next tokens");
     for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
   });
 }
@@ -853,6 +1011,7 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     ck(e, "graph instantiate");
     c->graph_batch = batch;
     c->graph_slots.assign(seq_ids, seq_ids + batch);
+    c->graph_cap_tokens = int64_t(io.max_splits) * io.split_tokens;
   });
 }
 
@@ -876,6 +1035,8 @@ int mmc_graph_run(mmc_ctx* c, int32_t n_steps, void* stream) {
     for (int s : c->graph_slots) {
       require(c->h_pos[s] + n_steps <= int64_t(c->h_pages[s]) * mmc::kPageTokens, MMC_ERR_NO_PAGES,
               "graph run needs more reserved KV pages (mmc_seq_reserve)");
+      require(c->h_pos[s] + n_steps <= c->graph_cap_tokens, MMC_ERR_STATE,
+              "graph run goes past the positions the graph was built for (rebuild it)");
       require(c->h_pos[s] + n_steps <= c->d.max_position_embeddings, MMC_ERR_OUT_OF_RANGE,
               "position exceeds max_position_embeddings");
     }
@@ -908,91 +1069,120 @@ int mmc_synchronize(mmc_ctx* c) {
   });
 }
 
-int mmc_kernels_per_step(const mmc_ctx* c, int32_t, int32_t* k) {
+int mmc_kernels_per_step(const mmc_ctx* c, int32_t batch, int32_t* k) {
   return guarded([&] {
     require(c && k, MMC_ERR_INVALID, "null argument");
-    *k = kernels_per_step(c);
+    *k = kernels_per_step(c, batch);
   });
 }
 
 // ------------------------------------------------------------- single ops
 
-int mmc_op_projection(int32_t batch, int32_t n, int32_t k, const void* w, const float* x, float* y, void* stream) {
+namespace {
+void op_init_attributes() {
+  static thread_local int done_dev = -1;
+  int dev = 0;
+  ck(cudaGetDevice(&dev), "device");
+  if (done_dev == dev) return;
+  ck(mmc::gemv_init_attributes(), "attributes");
+  ck(mmc::gemm_tc_init_attributes(), "attributes");
+  ck(mmc::attention_init_attributes(), "attributes");
+  done_dev = dev;
+}
+int current_sms() {
+  int dev = 0, sms = 148;
+  ck(cudaGetDevice(&dev), "device");
+  ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device query");
+  return sms;
+}
+}  // namespace
+
+int mmc_op_projection(int32_t batch, int32_t n, int32_t k, const void* w, const void* x, float* y, void* stream) {
   return guarded([&] {
     require(batch >= 1 && n > 0 && k > 0 && w && x && y, MMC_ERR_INVALID, "bad projection arguments");
-    require(batch <= 4 ? k % 8 == 0 : k % 64 == 0, MMC_ERR_INVALID, "k must be a multiple of 8 (batch<=4) or 64");
-    mmc::ProjArgs a;
-    a.W = static_cast<const __half*>(w);
-    a.N = n;
-    a.K = k;
-    a.B = batch;
-    a.in = x;
-    a.out = y;
-    a.ldo = n;
-    int dev = 0, sms = 148;
-    ck(cudaGetDevice(&dev), "device");
-    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device query");
-    static thread_local bool attrs = false;
-    if (!attrs) {
-      ck(mmc::gemv_init_attributes(), "attributes");
-      ck(mmc::gemm_init_attributes(), "attributes");
-      attrs = true;
-    }
+    require(batch <= kGemvMaxBatch ? k % 8 == 0 : k % 64 == 0, MMC_ERR_INVALID,
+            "k must be a multiple of 8 (batch <= 4) or 64 (batch > 4)");
+    op_init_attributes();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    ck(batch <= 4 ? mmc::launch_gemv(mmc::kProPlain, mmc::kEpiStore, a, sms, s, false)
-                  : mmc::launch_gemm(mmc::kProPlain, mmc::kEpiStore, a, s, false),
-       "projection launch");
+    if (batch <= kGemvMaxBatch) {
+      mmc::ProjArgs a;
+      a.W = static_cast<const __half*>(w);
+      a.N = n;
+      a.K = k;
+      a.B = batch;
+      a.in = static_cast<const float*>(x);
+      a.out = y;
+      a.ldo = n;
+      ck(mmc::launch_gemv(mmc::kProPlain, mmc::kEpiStore, a, current_sms(), s, false), "projection launch");
+    } else {
+      mmc::TcArgs t;
+      t.W = static_cast<const __half*>(w);
+      t.X = static_cast<const __half*>(x);
+      t.N = n;
+      t.K = k;
+      t.B = batch;
+      t.out = y;
+      t.ldo = n;
+      ck(mmc::launch_gemm_tc(mmc::kEpiStore, t, s, false), "projection launch");
+    }
   });
 }
 
 int mmc_op_lm_head_argmax_workspace_size(int32_t batch, int32_t n, int32_t k, size_t* bytes) {
   return guarded([&] {
     require(batch >= 1 && n > 0 && k > 0 && bytes, MMC_ERR_INVALID, "bad arguments");
-    int dev = 0, sms = 148;
-    ck(cudaGetDevice(&dev), "device");
-    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device query");
-    const size_t part = batch <= 4 ? mmc::gemv_argmax_part_bytes(n, k, batch, sms) : mmc::gemm_argmax_part_bytes(n, batch);
-    // partials | counters (batch tiles + 2) | token buffer | slots | positions
-    *bytes = (part + 255) / 256 * 256 + 256 * 4 + size_t(batch) * 4 * 3 + 256;
+    const size_t part = batch <= kGemvMaxBatch ? mmc::gemv_argmax_part_bytes(n, k, batch, current_sms())
+                                               : mmc::tc_argmax_part_bytes(n, batch);
+    // partials | counters | token buffer
+    *bytes = (part + 255) / 256 * 256 + size_t(mmc::tc_counter_words(n, batch) + 2) * 4 + size_t(batch) * 4 + 256;
   });
 }
 
-int mmc_op_lm_head_argmax(int32_t batch, int32_t n, int32_t k, const void* w, const float* x, float* logits,
+int mmc_op_lm_head_argmax(int32_t batch, int32_t n, int32_t k, const void* w, const void* x, float* logits,
                           int32_t* next, void* ws, size_t ws_bytes, void* stream) {
   return guarded([&] {
     size_t need = 0;
     if (mmc_op_lm_head_argmax_workspace_size(batch, n, k, &need) != MMC_OK) fail(MMC_ERR_INVALID, g_error);
     require(w && x && next && ws && ws_bytes >= need, MMC_ERR_INVALID, "bad arguments or workspace too small");
-    require(batch <= 4 ? k % 8 == 0 : k % 64 == 0, MMC_ERR_INVALID, "k must be a multiple of 8 (batch<=4) or 64");
-    int dev = 0, sms = 148;
-    ck(cudaGetDevice(&dev), "device");
-    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device query");
-    static thread_local bool attrs = false;
-    if (!attrs) {
-      ck(mmc::gemv_init_attributes(), "attributes");
-      ck(mmc::gemm_init_attributes(), "attributes");
-      attrs = true;
-    }
+    require(batch <= kGemvMaxBatch ? k % 8 == 0 : k % 64 == 0, MMC_ERR_INVALID,
+            "k must be a multiple of 8 (batch <= 4) or 64 (batch > 4)");
+    op_init_attributes();
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const size_t part = batch <= 4 ? mmc::gemv_argmax_part_bytes(n, k, batch, sms) : mmc::gemm_argmax_part_bytes(n, batch);
+    const size_t part = batch <= kGemvMaxBatch ? mmc::gemv_argmax_part_bytes(n, k, batch, current_sms())
+                                               : mmc::tc_argmax_part_bytes(n, batch);
     uint8_t* base = static_cast<uint8_t*>(ws);
+    const size_t words = size_t(mmc::tc_counter_words(n, batch) + 2);
     unsigned* counters = reinterpret_cast<unsigned*>(base + (part + 255) / 256 * 256);
-    int* tok = reinterpret_cast<int*>(base + (part + 255) / 256 * 256 + 256 * 4);
-    ck(cudaMemsetAsync(counters, 0, 256 * 4, s), "counter reset");
-    mmc::ProjArgs a;
-    a.W = static_cast<const __half*>(w);
-    a.N = n;
-    a.K = k;
-    a.B = batch;
-    a.in = x;
-    a.logits = logits;
-    a.argmax_part = base;
-    a.counter = counters;
-    a.sink.tokens = tok;
-    a.sink.next_out = next;
-    ck(batch <= 4 ? mmc::launch_gemv(mmc::kProPlain, mmc::kEpiArgmax, a, sms, s, false)
-                  : mmc::launch_gemm(mmc::kProPlain, mmc::kEpiArgmax, a, s, false),
-       "lm_head launch");
+    int* tok = reinterpret_cast<int*>(counters + words);
+    ck(cudaMemsetAsync(counters, 0, words * 4, s), "counter reset");
+    mmc::TokenSink sink;
+    sink.tokens = tok;
+    sink.next_out = next;
+    if (batch <= kGemvMaxBatch) {
+      mmc::ProjArgs a;
+      a.W = static_cast<const __half*>(w);
+      a.N = n;
+      a.K = k;
+      a.B = batch;
+      a.in = static_cast<const float*>(x);
+      a.logits = logits;
+      a.argmax_part = base;
+      a.counter = counters;
+      a.sink = sink;
+      ck(mmc::launch_gemv(mmc::kProPlain, mmc::kEpiArgmax, a, current_sms(), s, false), "lm_head launch");
+    } else {
+      mmc::TcArgs t;
+      t.W = static_cast<const __half*>(w);
+      t.X = static_cast<const __half*>(x);
+      t.N = n;
+      t.K = k;
+      t.B = batch;
+      t.logits = logits;
+      t.argmax_part = base;
+      t.counter = counters;
+      t.sink = sink;
+      ck(mmc::launch_gemm_tc(mmc::kEpiArgmax, t, s, false), "lm_head launch");
+    }
   });
 }
 
@@ -1016,11 +1206,7 @@ int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t
     size_t need = 0;
     if (mmc_op_attention_workspace_size(batch, nq, nkv, hd, max_ctx, &need) != MMC_OK) fail(MMC_ERR_INVALID, g_error);
     require(ws && ws_bytes >= need, MMC_ERR_INVALID, "workspace too small");
-    static thread_local bool attrs = false;
-    if (!attrs) {
-      ck(mmc::attention_init_attributes(), "attributes");
-      attrs = true;
-    }
+    op_init_attributes();
     const int pages = (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens;
     const int splits = std::min(64, pages);
     const int sp = (pages + splits - 1) / splits;

@@ -157,6 +157,18 @@ class DecodeEngine:
                                      logits.ctypes.data if want_logits else None))
         return nxt, logits
 
+    KERNEL_KINDS = ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "rmsnorm")
+
+    def profile_step(self, seq_ids, tokens):
+        """One step with per-kernel CUDA events; returns (next, {kind: (ms, launches)})."""
+        s, t = _i32(seq_ids), _i32(tokens)
+        nxt = np.empty_like(t)
+        ms = np.zeros(7, np.float32)
+        n = np.zeros(7, np.int32)
+        check(self.L.mmc_profile_step(self.h, len(s), s.ctypes.data, t.ctypes.data, nxt.ctypes.data, ms.ctypes.data,
+                                      n.ctypes.data))
+        return nxt, {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.KERNEL_KINDS)}
+
     def step_async(self, seq_ids, d_tokens: int, d_next: int, d_logits: int | None = None, stream: int | None = None):
         s = _i32(seq_ids)
         check(self.L.mmc_decode_step_async(self.h, len(s), s.ctypes.data, d_tokens, d_next, d_logits, stream))

@@ -24,13 +24,15 @@ def dev(t):
 
 
 @pytest.mark.parametrize("n,k", SWEEP_SHAPES)
-@pytest.mark.parametrize("batch", [1, 3, 8, 64, 256])
+@pytest.mark.parametrize("batch", [1, 3, 5, 8, 64, 100, 256])
 def test_projection(n, k, batch):
     g = torch.Generator(device="cpu").manual_seed(n * 7 + k + batch)
     w = (torch.randn(n, k, generator=g) * 0.02).half().cuda()
     x = torch.randn(batch, k, generator=g).cuda()
     y = torch.full((batch, n), float("nan"), device="cuda")
-    check(lib().mmc_op_projection(batch, n, k, dev(w), dev(x), dev(y), None))
+    # fp32 activations for the CUDA-core path (batch <= 4), fp16 for tcgen05
+    xa = x if batch <= 4 else x.half().contiguous()
+    check(lib().mmc_op_projection(batch, n, k, dev(w), dev(xa), dev(y), None))
     torch.cuda.synchronize()
     # batches > 4 run on tensor cores with fp16 activations; <= 4 in fp32
     xr = x if batch <= 4 else x.half().float()
@@ -55,8 +57,9 @@ def test_lm_head_argmax_is_first_max_of_its_own_logits(batch):
     ws_bytes = C.c_size_t()
     check(lib().mmc_op_lm_head_argmax_workspace_size(batch, n, k, C.byref(ws_bytes)))
     ws = torch.empty(ws_bytes.value, dtype=torch.uint8, device="cuda")
+    xa = x if batch <= 4 else x.half().contiguous()
     for _ in range(3):  # repeated launches: the arrival counters must self-reset
-        check(lib().mmc_op_lm_head_argmax(batch, n, k, dev(w), dev(x), dev(logits), dev(nxt), dev(ws),
+        check(lib().mmc_op_lm_head_argmax(batch, n, k, dev(w), dev(xa), dev(logits), dev(nxt), dev(ws),
                                           ws_bytes.value, None))
     torch.cuda.synchronize()
     lg = logits.cpu().numpy()
@@ -75,6 +78,8 @@ def test_lm_head_argmax_tie_goes_to_lowest_index():
     w = w.cuda()
     for batch in (1, 4, 16):
         x = torch.ones(batch, k, device="cuda")
+        if batch > 4:
+            x = x.half()
         nxt = torch.full((batch,), -1, dtype=torch.int32, device="cuda")
         ws_bytes = C.c_size_t()
         check(lib().mmc_op_lm_head_argmax_workspace_size(batch, n, k, C.byref(ws_bytes)))
