@@ -117,6 +117,12 @@ MMC_EXPORT int mmc_seq_position(const mmc_ctx* ctx, int32_t seq, int64_t* positi
  * ([position][kv_head][head_dim], decoder_layer.h:40-48). */
 MMC_EXPORT int mmc_debug_read_kv(mmc_ctx* ctx, int32_t seq, int32_t layer, float* keys_host, float* values_host);
 
+/* Benchmark helper: mark the first `n_tokens` positions of an empty sequence
+ * as cached and fill them with seeded pseudo-random fp16 K/V (all layers), so
+ * decode steps can be timed at a long context without an O(n) prompt pass.
+ * Decode cost does not depend on the cached values. */
+MMC_EXPORT int mmc_debug_fill_kv(mmc_ctx* ctx, int32_t seq, int64_t n_tokens, uint32_t seed);
+
 /* Test helper: copy a per-step scratch buffer of the last step to host fp32:
  * which = 0 residual stream [batch][hidden], 1 raw q|k|v projections
  * [batch][(nq + 2 nkv) * hd], 2 attention output [batch][nq * hd],

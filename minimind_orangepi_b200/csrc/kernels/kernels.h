@@ -148,6 +148,8 @@ cudaError_t attention_init_attributes();
 // Weight packing: fp32 source rows -> fp16 destination rows (RNE), with an
 // optional gate/up interleave by blocks of 8 rows.
 cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s);
+cudaError_t launch_fill_kv(__half* pool, const int* pages, int n_tokens, int64_t page_halves, int row_halves,
+                           uint32_t seed, cudaStream_t s);
 cudaError_t launch_pack_gate_up(const float* gate, const float* up, __half* dst, int64_t inter, int64_t cols,
                                 cudaStream_t s);
 

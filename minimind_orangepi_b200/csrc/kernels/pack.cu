@@ -32,7 +32,35 @@ __global__ void pack_gate_up_kernel(const float* __restrict__ gate, const float*
   }
 }
 
+// Seeded pseudo-random fp16 values in [-2, 2) for positions [0, n) of one
+// sequence's pages (all layers, K and V). A 32-bit integer hash of the element
+// index gives reproducible contents.
+__global__ void fill_kv_kernel(__half* pool, const int* pages, int n_tokens, int64_t page_halves, int row_halves,
+                               uint32_t seed) {
+  const int64_t total = int64_t((n_tokens + 63) / 64) * page_halves;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int p = int(i / page_halves);
+    const int64_t off = i % page_halves;
+    const int row = int((off / row_halves) % 64);
+    if (p * 64 + row >= n_tokens) continue;
+    uint32_t x = uint32_t(i) * 0x9E3779B9u ^ seed;
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    const float v = float(x & 0xFFFF) * (4.0f / 65536.0f) - 2.0f;
+    pool[int64_t(pages[p]) * page_halves + off] = __float2half_rn(v);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_fill_kv(__half* pool, const int* pages, int n_tokens, int64_t page_halves, int row_halves,
+                           uint32_t seed, cudaStream_t s) {
+  fill_kv_kernel<<<592, 256, 0, s>>>(pool, pages, n_tokens, page_halves, row_halves, seed);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s) {
   pack_rows_kernel<<<1184, 256, 0, s>>>(src, dst, rows * cols);

@@ -841,6 +841,26 @@ int mmc_debug_read_kv(mmc_ctx* c, int32_t seq, int32_t layer, float* keys, float
   });
 }
 
+int mmc_debug_fill_kv(mmc_ctx* c, int32_t seq, int64_t n_tokens, uint32_t seed) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    require_ready(c);
+    use_device(c);
+    check_seq(c, seq);
+    require(c->h_pos[seq] == 0, MMC_ERR_STATE, "fill needs an empty sequence");
+    require(n_tokens >= 0 && n_tokens < c->d.max_position_embeddings, MMC_ERR_OUT_OF_RANGE,
+            "n_tokens outside [0, max_position_embeddings)");
+    reserve_pages(c, seq, std::max<int64_t>(n_tokens + 1, 1));
+    if (n_tokens > 0)
+      ck(mmc::launch_fill_kv(c->kv_pool, c->d_block_table + size_t(seq) * c->max_pages, int(n_tokens),
+                             c->page_halves, int(c->d.head_dim), seed, c->stream),
+         "fill launch");
+    const int pos = int(n_tokens);
+    upload(c, c->d_seq_pos + seq, &pos, sizeof(int), "position");
+    c->h_pos[seq] = n_tokens;
+  });
+}
+
 int mmc_debug_scratch(mmc_ctx* c, int32_t which, float* host, int64_t count) {
   return guarded([&] {
     require(c && host && count >= 0, MMC_ERR_INVALID, "null argument");

@@ -133,6 +133,11 @@ class DecodeEngine:
         check(self.L.mmc_seq_position(self.h, seq, C.byref(p)))
         return p.value
 
+    def fill_context(self, seq: int, n_tokens: int, seed: int = 0) -> None:
+        """Fast-forward an empty sequence to `n_tokens` cached positions of
+        seeded synthetic K/V (benchmarks and profiling only)."""
+        check(self.L.mmc_debug_fill_kv(self.h, seq, n_tokens, seed))
+
     def page_bytes(self) -> int:
         b = C.c_int64()
         check(self.L.mmc_kv_page_bytes(self.h, C.byref(b)))
