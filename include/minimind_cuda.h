@@ -211,6 +211,21 @@ MMC_EXPORT int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t 
                      const int32_t* d_block_table, int32_t max_pages, const int32_t* d_seq_pos,
                      const int32_t* d_slots, int32_t max_ctx, float* d_out, void* d_workspace,
                      size_t workspace_bytes, void* stream);
+/* mmc_op_attention without a workspace argument, for callers that cannot
+ * allocate device memory (no cudaMalloc where they run: allocator hooks, host
+ * callbacks, hosts that own all device memory). No counterpart in the
+ * reference. The scratch is a fixed 16 MiB array inside the library that every
+ * GPU loading it keeps until exit; sizes needing more scratch than that (see
+ * mmc_op_attention_workspace_size) fail with MMC_ERR_INVALID. The first call on
+ * a device looks up the array's address with that device current (make it
+ * before any stream capture). The array is shared by all calls: calls that
+ * overlap on the GPU race. Allocates nothing. */
+MMC_EXPORT int mmc_op_attention_noalloc(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t layer,
+                                        int32_t layers, const float* d_qkv, const float* d_q_norm,
+                                        const float* d_k_norm, const float* d_rope_cos, const float* d_rope_sin,
+                                        int32_t max_pos, float eps, void* d_kv_pool, const int32_t* d_block_table,
+                                        int32_t max_pages, const int32_t* d_seq_pos, const int32_t* d_slots,
+                                        int32_t max_ctx, float* d_out, void* stream);
 /* Element offset (in halves) of (row, 16-byte chunk) inside one 64 x hd page
  * slab: the cache's swizzled row layout, for tools that read pages directly. */
 MMC_EXPORT int64_t mmc_kv_row_offset(int32_t hd, int32_t row, int32_t chunk);

@@ -38,6 +38,7 @@ CUDA_SOURCES = [
     CSRC / "kernels" / "attention.cu",
     CSRC / "kernels" / "pack.cu",
     CSRC / "mmc_api.cu",
+    CSRC / "attention_noalloc.cu",
 ]
 RUNTIME_SOURCES = [
     CSRC / "runtime" / "config.cpp",

@@ -591,6 +591,8 @@ void drop_graph(mmc_ctx* c) {
 
 }  // namespace
 
+void mmc_set_last_error(const std::string& msg) { g_error = msg; }
+
 extern "C" {
 
 const char* mmc_last_error(void) { return g_error.c_str(); }
