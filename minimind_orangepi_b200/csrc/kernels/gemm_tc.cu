@@ -3,18 +3,22 @@
 // Y^T[n][b] = W[n][:] . X[b][:]: the weight rows are the UMMA M side (128 per
 // CTA), the batch rows the N side (BN per CTA), K runs in 64-element steps.
 // Operands are fp16 in HBM/L2 (W packed at load time, X written fp16 by the
-// producer kernel), copied with 16-byte cp.async into shared-memory tiles laid
-// out as the canonical K-major SWIZZLE_128B atoms (8 rows x 128 B, 16-byte
-// chunks XOR-ed with the row), so each tile is directly a UMMA smem operand.
-// One elected thread issues tcgen05.mma (fp32 accumulate in TMEM) and commits
-// each stage to an mbarrier that frees the stage for the next copy. The
-// epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
-// 32w..32w+31 = weight rows) and fuses the store / residual add / SiLU*mul /
-// argmax of the decode step.
+// producer kernel). Warp-specialised pipeline, no block-wide barrier in the K
+// loop:
+//   warp 0 / lane 0  TMA producer: 2-D tensor-map loads (128-byte swizzle, the
+//                    canonical UMMA K-major SW128 layout) into a ring of
+//                    stages; full[s] completes on the transaction bytes; the
+//                    first stages' weight tiles are issued before
+//                    griddepcontrol.wait;
+//   warp 1 / lane 0  MMA issuer: waits full[s], issues tcgen05.mma (fp32
+//                    accumulate in TMEM), commits empty[s] to free the stage
+//                    and finally `done`;
+//   all 4 warps      epilogue: tcgen05.ld of the accumulator (warp w owns TMEM
+//                    lanes 32w..32w+31 = weight rows) fused with the store /
+//                    residual add / SiLU*mul / argmax of the decode step.
 //
-// Every wait is bounded (2 s): on timeout the kernel records an error, waits
-// for its own outstanding copies and MMAs as far as it can, frees its TMEM and
-// returns.
+// Every wait is bounded (2 s): on timeout the kernel records an error, frees
+// its TMEM and returns.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -24,7 +28,13 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int UM = 128;       // UMMA M (weight rows per CTA)
 constexpr int BK = 64;        // K per stage (one 128-byte swizzle atom of fp16)
-constexpr int NSTAGE = 4;
+// Stage ring depth per batch tile (about 160 KB of tiles); loads run
+// PD = NSTAGE - 2 tiles ahead, so the stage being refilled belongs to the MMA
+// issued two iterations earlier and the copy never waits on the newest MMA.
+template <int BN>
+constexpr int stages_for() {
+  return BN >= 256 ? 4 : (BN >= 128 ? 5 : 8);
+}
 
 struct ArgBest {
   float v;
@@ -32,11 +42,6 @@ struct ArgBest {
 };
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return (v > bv) || (v == bv && i < bi); }
 
-__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ int tile_off(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
 // K-major SWIZZLE_128B shared-memory matrix descriptor (tile base 1024-aligned):
 // start>>4 | LBO (16 B)>>4 << 16 | SBO (1024 B)>>4 << 32 | version 1 << 46 | layout 2 << 61
@@ -79,13 +84,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads) gemm_tc_kernel(TcArgs a) {
+__global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant__ TcArgs a) {
+  constexpr int NSTAGE = stages_for<BN>();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-align the stage ring (SWIZZLE_128B atoms)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int A_BYTES = UM * BK * 2, B_BYTES = BN * BK * 2, ST_BYTES = A_BYTES + B_BYTES;
-  __shared__ __align__(8) uint64_t mma_bar[NSTAGE];
+  __shared__ __align__(8) uint64_t full_bar[8];
+  __shared__ __align__(8) uint64_t empty_bar[8];
+  __shared__ __align__(8) uint64_t done_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
   __shared__ ArgBest best_s[4][BN];
@@ -93,41 +109,23 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(TcArgs a) {
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int m0 = blockIdx.x * UM, n0 = blockIdx.y * BN;
-  const int K = a.K, KT = K / BK;
+  const int KT = a.K / BK;
+  const int pre = KT < NSTAGE ? KT : NSTAGE;
 
   if (tid == 0) {
     abort_flag = 0;
-    for (int s = 0; s < NSTAGE; ++s) mbar_init(&mma_bar[s], 1);
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&done_bar, 1);
     fence_mbar_init();
+    // weight tiles do not depend on the previous kernel: start them now
+    for (int s = 0; s < pre; ++s) {
+      mbar_arrive_expect_tx(&full_bar[s], uint32_t(ST_BYTES));
+      tma_load_2d(smem + s * ST_BYTES, &a.map_w, s * BK, m0, &full_bar[s]);
+    }
   }
-
-  auto load_a = [&](int kt) {  // weights: independent of the previous kernel
-    uint8_t* as = smem + (kt % NSTAGE) * ST_BYTES;
-#pragma unroll
-    for (int i = 0; i < (UM * 8) / kThreads; ++i) {
-      const int idx = tid + i * kThreads;
-      const int r = idx >> 3, c = idx & 7;
-      const bool ok = m0 + r < a.N;
-      cp_async16_zfill(as + tile_off(r, c), a.W + size_t(ok ? m0 + r : 0) * K + kt * BK + c * 8, ok);
-    }
-  };
-  auto load_b = [&](int kt) {  // activations: produced by the previous kernel
-    uint8_t* bs = smem + (kt % NSTAGE) * ST_BYTES + A_BYTES;
-#pragma unroll
-    for (int i = 0; i < (BN * 8 + kThreads - 1) / kThreads; ++i) {
-      const int idx = tid + i * kThreads;
-      if (idx < BN * 8) {
-        const int r = idx >> 3, c = idx & 7;
-        const bool ok = n0 + r < a.B;
-        cp_async16_zfill(bs + tile_off(r, c), a.X + size_t(ok ? n0 + r : 0) * K + kt * BK + c * 8, ok);
-      }
-    }
-  };
-
-  // prefetch the first weight stages before waiting on the previous kernel
-#pragma unroll
-  for (int s = 0; s < NSTAGE - 1; ++s)
-    if (s < KT) load_a(s);
   __syncthreads();
   pdl_wait();
   if (warp == 0) {
@@ -137,53 +135,50 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(TcArgs a) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   pdl_launch_dependents();
-  // one commit group per prefetched stage: A (issued above) + B
-#pragma unroll
-  for (int s = 0; s < NSTAGE - 1; ++s) {
-    if (s < KT) load_b(s);
-    cp_async_commit();
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
-  const uint32_t idesc = idesc_f16<BN>();
 
-  for (int kt = 0; kt < KT; ++kt) {
-    // stage (kt + NSTAGE - 1) % NSTAGE was last read by the MMAs of kt - 1
-    const int pf = kt + NSTAGE - 1;
-    if (pf < KT) {
-      if (kt >= 1) {
-        const int prev = kt - 1;
-        if (!mbar_wait_bounded(&mma_bar[prev % NSTAGE], (prev / NSTAGE) & 1, a.err)) abort_flag = 1;
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      for (int s = 0; s < pre; ++s) tma_load_2d(smem + s * ST_BYTES + A_BYTES, &a.map_x, s * BK, n0, &full_bar[s]);
+      for (int kt = pre; kt < KT; ++kt) {
+        const int s = kt % NSTAGE;
+        if (!mbar_wait_bounded(&empty_bar[s], ((kt / NSTAGE) - 1) & 1, a.err)) {
+          abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[s], uint32_t(ST_BYTES));
+        tma_load_2d(smem + s * ST_BYTES, &a.map_w, kt * BK, m0, &full_bar[s]);
+        tma_load_2d(smem + s * ST_BYTES + A_BYTES, &a.map_x, kt * BK, n0, &full_bar[s]);
       }
-      load_a(pf);
-      load_b(pf);
     }
-    cp_async_commit();
-    cp_async_wait<NSTAGE - 1>();  // this thread's copies for stage kt have landed
-    fence_proxy_async_smem();     // make them visible to the tensor-core (async) proxy
-    __syncthreads();
-    if (abort_flag) break;
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t as = smem_u32(smem + (kt % NSTAGE) * ST_BYTES);
-      const uint32_t bs = as + A_BYTES;
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      const uint32_t idesc = idesc_f16<BN>();
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % NSTAGE;
+        if (!mbar_wait_bounded(&full_bar[s], (kt / NSTAGE) & 1, a.err)) {
+          abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t as = smem_u32(smem + s * ST_BYTES);
+        const uint32_t bs = as + A_BYTES;
 #pragma unroll
-      for (int k = 0; k < BK / 16; ++k)
-        umma_f16(tmem, sw128_desc(as + k * 32), sw128_desc(bs + k * 32), idesc, (kt | k) != 0);
-      umma_commit(&mma_bar[kt % NSTAGE]);
+        for (int k = 0; k < BK / 16; ++k)
+          umma_f16(tmem, sw128_desc(as + k * 32), sw128_desc(bs + k * 32), idesc, (kt | k) != 0);
+        umma_commit(&empty_bar[s]);
+      }
+      umma_commit(&done_bar);  // arrives once every MMA above has completed
     }
+    __syncwarp();
   }
-  cp_async_wait<0>();
-  // all MMAs done: the last commit covers every earlier tcgen05.mma of thread 0
-  if (!abort_flag && KT > 0) {
-    const int last = KT - 1;
-    if (!mbar_wait_bounded(&mma_bar[last % NSTAGE], (last / NSTAGE) & 1, a.err)) abort_flag = 1;
-  }
-  tc_fence_before();
-  __syncthreads();
+  if (!mbar_wait_bounded(&done_bar, 0, a.err)) abort_flag = 1;
   tc_fence_after();
+  __syncthreads();
 
   ArgBest bst[BN / 16 > 0 ? BN / 16 : 1];
   if (!abort_flag) {
@@ -349,7 +344,7 @@ __global__ void __launch_bounds__(256) rmsnorm_f16_kernel(NormArgs a) {
 
 template <int BN>
 constexpr size_t tc_smem() {
-  return size_t(NSTAGE) * (UM * BK * 2 + BN * BK * 2) + 1024;
+  return size_t(stages_for<BN>()) * (UM * BK * 2 + BN * BK * 2) + 1024;
 }
 
 template <int BN, int EPI>
@@ -367,10 +362,47 @@ cudaError_t launch_bn(const TcArgs& a, cudaStream_t s, bool pdl) {
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI>, a);
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D fp16 [rows][K] row-major tensor, boxes of 64 (K) x box_rows, 128-byte
+// swizzle (the UMMA SW128 K-major layout); rows past `rows` read as zero.
+cudaError_t make_map(CUtensorMap* m, const __half* base, int rows, int K, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+  const cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 template <int EPI>
-cudaError_t launch_epi(const TcArgs& a, cudaStream_t s, bool pdl) {
-  const int bn = tc_batch_tile(a.N, a.B);
+cudaError_t launch_epi(const TcArgs& a_in, cudaStream_t s, bool pdl) {
+  const int bn = tc_batch_tile(a_in.N, a_in.B);
+  TcArgs a = a_in;
+  cudaError_t e = make_map(&a.map_w, a.W, a.N, a.K, UM);
+  if (e != cudaSuccess) return e;
+  e = make_map(&a.map_x, a.X, a.B, a.K, bn);
+  if (e != cudaSuccess) return e;
   switch (bn) {
+    case 16: return launch_bn<16, EPI>(a, s, pdl);
     case 32: return launch_bn<32, EPI>(a, s, pdl);
     case 64: return launch_bn<64, EPI>(a, s, pdl);
     case 128: return launch_bn<128, EPI>(a, s, pdl);
@@ -403,19 +435,19 @@ cudaError_t attrs_bn() {
 // else 32 (small problems are latency-bound; more CTAs help).
 int tc_batch_tile(int N, int B) {
   const int mt = (N + UM - 1) / UM;
-  for (int bn : {256, 128, 64}) {
+  for (int bn : {256, 128, 64, 32}) {
     if (bn > 2 * B) continue;
     if (mt * ((B + bn - 1) / bn) >= 148) return bn;
   }
-  return B <= 32 ? 32 : (B <= 64 ? 32 : 32);
+  return 16;
 }
 
 size_t tc_argmax_part_bytes(int N, int B) { return size_t(B) * ((N + UM - 1) / UM) * sizeof(ArgBest); }
-int tc_counter_words(int N, int B) { return (B + 31) / 32 + 2; }
+int tc_counter_words(int N, int B) { return (B + 15) / 16 + 2; }
 
 cudaError_t gemm_tc_init_attributes() {
   cudaError_t e1 = attrs_bn<32>(), e2 = attrs_bn<64>(), e3 = attrs_bn<128>(), e4 = attrs_bn<256>();
-  cudaError_t e5 = cudaSuccess;
+  cudaError_t e5 = attrs_bn<16>();
   return e1 != cudaSuccess ? e1 : e2 != cudaSuccess ? e2 : e3 != cudaSuccess ? e3 : e4 != cudaSuccess ? e4 : e5;
 }
 

@@ -4,6 +4,7 @@
 // overlaps the tail of the kernel before it.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -80,6 +81,8 @@ cudaError_t gemv_init_attributes();
 // Tensor-core projection for batches B > 4 (tcgen05.mma, fp16 operands, fp32
 // accumulate in TMEM): weight rows on the UMMA M side, batch rows on N.
 struct TcArgs {
+  CUtensorMap map_w;  // filled by launch_gemm_tc (TMA descriptors of W and X)
+  CUtensorMap map_x;
   const __half* W = nullptr;  // [N][K] fp16
   const __half* X = nullptr;  // [B][K] fp16 activations
   int N = 0, K = 0, B = 0;
@@ -148,6 +151,7 @@ cudaError_t attention_init_attributes();
 // Weight packing: fp32 source rows -> fp16 destination rows (RNE), with an
 // optional gate/up interleave by blocks of 8 rows.
 cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s);
+cudaError_t launch_hold(uint64_t ns, cudaStream_t s);
 cudaError_t launch_fill_kv(__half* pool, const int* pages, int n_tokens, int64_t page_halves, int row_halves,
                            uint32_t seed, cudaStream_t s);
 cudaError_t launch_pack_gate_up(const float* gate, const float* up, __half* dst, int64_t inter, int64_t cols,

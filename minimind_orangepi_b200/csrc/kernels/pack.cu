@@ -54,7 +54,25 @@ __global__ void fill_kv_kernel(__half* pool, const int* pages, int n_tokens, int
   }
 }
 
+// Keeps the GPU busy for about `ns` nanoseconds (bounded by the global timer)
+// so that host-side enqueueing finishes before timed work starts.
+__global__ void hold_kernel(uint64_t ns) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  uint64_t t = t0;
+  while (t - t0 < ns) {
+    __nanosleep(1000);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_hold(uint64_t ns, cudaStream_t s) {
+  if (ns > 100000000ull) ns = 100000000ull;  // at most 0.1 s
+  hold_kernel<<<1, 1, 0, s>>>(ns);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_fill_kv(__half* pool, const int* pages, int n_tokens, int64_t page_halves, int row_halves,
                            uint32_t seed, cudaStream_t s) {

@@ -173,14 +173,19 @@ void check_device_error(mmc_ctx* c) {
 
 // Split size for the attention kernel: enough CTAs to cover the SMs a few
 // times over, at most `max_splits_cap` splits per sequence.
-int plan_split(const mmc_ctx* c, int64_t total_pages, int64_t max_ctx, int* max_splits) {
+int plan_split_raw(int64_t total_pages, int64_t nkv, int num_sms, int cap, int64_t max_ctx, int* max_splits) {
   const int64_t pages = std::max<int64_t>(1, (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens);
-  int64_t sp = std::max<int64_t>(1, total_pages * c->d.num_key_value_heads / (4 * c->num_sms));
-  sp = std::max<int64_t>(sp, (pages + c->max_splits_cap - 1) / c->max_splits_cap);
+  int64_t sp = std::max<int64_t>(1, total_pages * nkv / (4 * num_sms));
+  sp = std::max<int64_t>(sp, (pages + cap - 1) / cap);
   sp = std::min<int64_t>(sp, pages);
   *max_splits = int((pages + sp - 1) / sp);
   return int(sp * mmc::kPageTokens);
 }
+
+int plan_split(const mmc_ctx* c, int64_t total_pages, int64_t max_ctx, int* max_splits) {
+  return plan_split_raw(total_pages, c->d.num_key_value_heads, c->num_sms, c->max_splits_cap, max_ctx, max_splits);
+}
+
 
 struct StepIO {
   int B = 0;
@@ -939,6 +944,9 @@ int mmc_profile_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const in
     std::vector<int> kinds;
     for (auto& e : ev) ck(cudaEventCreate(&e), "event create");
     try {
+      // hold the stream while the host enqueues the step, so the event gaps
+      // measure device time rather than host launch latency
+      ck(mmc::launch_hold(uint64_t(n) * 20000ull, c->stream), "hold launch");
       enqueue_step(c, io, c->stream, ev.data(), &kinds);
       ck(cudaStreamSynchronize(c->stream), "profiled step");
       check_device_error(c);
@@ -1229,9 +1237,11 @@ int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t
     if (mmc_op_attention_workspace_size(batch, nq, nkv, hd, max_ctx, &need) != MMC_OK) fail(MMC_ERR_INVALID, g_error);
     require(ws && ws_bytes >= need, MMC_ERR_INVALID, "workspace too small");
     op_init_attributes();
-    const int pages = (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens;
-    const int splits = std::min(64, pages);
-    const int sp = (pages + splits - 1) / splits;
+    // same split planner as the decode step; at most 64 splits, so the
+    // workspace size above stays an upper bound
+    const int64_t pages = (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens;
+    int max_splits = 1;
+    const int split_tokens = plan_split_raw(int64_t(batch) * pages, nkv, current_sms(), 64, max_ctx, &max_splits);
     mmc::AttnArgs a;
     a.qkv = qkv;
     a.ld_qkv = (nq + 2 * nkv) * hd;
@@ -1252,11 +1262,13 @@ int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t
     a.nq = nq;
     a.nkv = nkv;
     a.hd = hd;
-    a.split_tokens = sp * mmc::kPageTokens;
-    a.max_splits = (pages + sp - 1) / sp;
+    a.split_tokens = split_tokens;
+    a.max_splits = max_splits;
     a.out = out;
     uint8_t* base = static_cast<uint8_t*>(ws);
-    const size_t pbytes = (mmc::attn_part_floats(batch, nkv, splits, nq / nkv, hd) * 4 + 255) / 256 * 256;
+    // workspace layout as sized by mmc_op_attention_workspace_size
+    const int splits_ws = int(std::min<int64_t>(64, pages));
+    const size_t pbytes = (mmc::attn_part_floats(batch, nkv, splits_ws, nq / nkv, hd) * 4 + 255) / 256 * 256;
     a.part = reinterpret_cast<float*>(base);
     a.counters = reinterpret_cast<unsigned*>(base + pbytes);
     a.err = reinterpret_cast<int*>(base + pbytes + size_t(batch) * nkv * 4);

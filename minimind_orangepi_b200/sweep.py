@@ -2,7 +2,7 @@
 points, timed with CUDA events on the launch stream.
 
   python -m minimind_orangepi_b200.sweep [--case projection|attention|lm_head|all]
-      [--batch B ...] [--ctx C ...] [--hd D ...] [--iters N] [--no-flush] [--json]
+      [--batch B ...] [--ctx C ...] [--hd D ...] [--shape NxK ...] [--iters N] [--json]
 
 (a) projections [N x K] in {512x512, 128x512, 1408x512, 512x1408, 768x768,
     192x768, 2048x768, 768x2048, 6400x768} at batch 1, 8, 64, 256 (weights
@@ -13,8 +13,10 @@ points, timed with CUDA events on the launch stream.
 (c) lm_head 6400 x 768 + argmax.
 Each line reports the kernel's algorithmic bytes (and FLOPs) per launch, the
 mean launch time and the fraction of the measured HBM / tensor peaks
-(MEASURED_PEAKS.json). Between timed launches a 256 MB buffer is rewritten so
-each launch starts with a cold L2, unless --no-flush.
+(MEASURED_PEAKS.json). Launches run back to back between two CUDA events
+after a warm-up; projection weights rotate over enough copies (> 3x L2) that
+every launch streams them from HBM; the attention cases that matter exceed L2
+on their own.
 """
 from __future__ import annotations
 
@@ -28,6 +30,7 @@ import numpy as np
 from ._lib import check, lib
 
 ROOT = Path(__file__).resolve().parents[1]
+L2_BYTES = 126 * 2**20
 PROJ_SHAPES = [(512, 512), (128, 512), (1408, 512), (512, 1408), (768, 768), (192, 768), (2048, 768), (768, 2048),
                (6400, 768)]
 
@@ -39,31 +42,35 @@ def _peaks():
 
 
 class Timer:
-    def __init__(self, torch, iters: int, flush: bool):
+    """Back-to-back launches between two CUDA events on one stream, after a
+    warm-up that brings the clocks up. Callers rotate over enough copies of
+    their inputs that each launch reads from HBM, not L2."""
+
+    def __init__(self, torch, iters: int):
         self.torch = torch
         self.iters = iters
-        self.flush = flush
-        self.scratch = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda") if flush else None
         self.stream = torch.cuda.Stream()
 
     def run(self, fn) -> float:
-        """Mean ms of fn(stream_ptr) over `iters` launches after 3 warm-ups."""
+        """Mean ms per launch of fn(stream_ptr, i) for i in range(iters)."""
         t = self.torch
         sp = self.stream.cuda_stream
         with t.cuda.stream(self.stream):
-            for _ in range(3):
-                fn(sp)
-            total = 0.0
-            for _ in range(self.iters):
-                if self.flush:
-                    self.scratch.fill_(1)
-                e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
-                e0.record(self.stream)
-                fn(sp)
-                e1.record(self.stream)
-                e1.synchronize()
-                total += e0.elapsed_time(e1)
-        return total / self.iters
+            for i in range(max(3, self.iters // 4)):
+                fn(sp, i)
+            t.cuda._sleep(2_000_000)  # let the host run ahead of the device
+            e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+            for i in range(self.iters):
+                fn(sp, i)
+            e1.record(self.stream)
+            e1.synchronize()
+        return e0.elapsed_time(e1) / self.iters
+
+
+def copies_for(bytes_per_set: int) -> int:
+    """Input sets needed so consecutive launches never find their data in L2."""
+    return max(1, min(64, (3 * L2_BYTES) // max(bytes_per_set, 1) + 1))
 
 
 def dev(t):
@@ -75,12 +82,15 @@ def sweep_projection(torch, timer, batches, shapes):
     out = []
     for n, k in shapes:
         g = torch.Generator(device="cpu").manual_seed(n + k)
-        w = (torch.randn(n, k, generator=g) * 0.02).half().cuda()
+        ncp = copies_for(2 * n * k)
+        w0 = (torch.randn(n, k, generator=g) * 0.02).half().cuda()
+        ws = [w0.clone() for _ in range(ncp)]
         for b in batches:
             x = torch.randn(b, k, generator=g).cuda()
             xa = x if b <= 4 else x.half().contiguous()
             y = torch.empty(b, n, device="cuda")
-            ms = timer.run(lambda s: check(lib().mmc_op_projection(b, n, k, dev(w), dev(xa), dev(y), C.c_void_p(s))))
+            ms = timer.run(lambda s, i: check(lib().mmc_op_projection(b, n, k, dev(ws[i % ncp]), dev(xa), dev(y),
+                                                                      C.c_void_p(s))))
             bytes_ = 2 * n * k + xa.element_size() * b * k + 4 * b * n
             flops = 2 * b * n * k
             gbs, tfl = bytes_ / ms / 1e6, flops / ms / 1e9
@@ -125,7 +135,7 @@ def sweep_attention(torch, timer, batches, ctxs, hds, nq=8, nkv=2):
                 check(lib().mmc_op_attention_workspace_size(b, nq, nkv, hd, ctx, C.byref(ws_n)))
                 ws = torch.empty(ws_n.value, dtype=torch.uint8, device="cuda")
 
-                def fn(s):
+                def fn(s, i):
                     check(lib().mmc_op_attention(b, nq, nkv, hd, 0, 1, dev(qkv), dev(qn), dev(kn), dev(cos), dev(sin),
                                                  ctx, 1e-5, dev(pool), dev(bt), max_pages, dev(pos), dev(slots), ctx,
                                                  dev(o), dev(ws), ws_n.value, C.c_void_p(s)))
@@ -141,7 +151,9 @@ def sweep_attention(torch, timer, batches, ctxs, hds, nq=8, nkv=2):
 def sweep_lm_head(torch, timer, batches, n=6400, k=768):
     hbm, tc, src = _peaks()
     out = []
-    w = (torch.randn(n, k) * 0.02).half().cuda()
+    ncp = copies_for(2 * n * k)
+    w0 = (torch.randn(n, k) * 0.02).half().cuda()
+    wl = [w0.clone() for _ in range(ncp)]
     for b in batches:
         x = torch.randn(b, k, device="cuda")
         xa = x if b <= 4 else x.half().contiguous()
@@ -149,8 +161,8 @@ def sweep_lm_head(torch, timer, batches, n=6400, k=768):
         ws_n = C.c_size_t()
         check(lib().mmc_op_lm_head_argmax_workspace_size(b, n, k, C.byref(ws_n)))
         ws = torch.empty(ws_n.value, dtype=torch.uint8, device="cuda")
-        ms = timer.run(lambda s: check(lib().mmc_op_lm_head_argmax(b, n, k, dev(w), dev(xa), None, dev(nxt), dev(ws),
-                                                                   ws_n.value, C.c_void_p(s))))
+        ms = timer.run(lambda s, i: check(lib().mmc_op_lm_head_argmax(b, n, k, dev(wl[i % ncp]), dev(xa), None,
+                                                                      dev(nxt), dev(ws), ws_n.value, C.c_void_p(s))))
         bytes_ = 2 * n * k + xa.element_size() * b * k + 4 * b
         gbs = bytes_ / ms / 1e6
         out.append({"case": "lm_head_argmax", "n": n, "k": k, "batch": b, "ms": ms, "bytes": bytes_, "GB/s": gbs,
@@ -164,15 +176,16 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, nargs="*")
     ap.add_argument("--ctx", type=int, nargs="*")
     ap.add_argument("--hd", type=int, nargs="*")
+    ap.add_argument("--shape", type=str, nargs="*", help="projection shapes as NxK (default: the config-5 list)")
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--no-flush", action="store_true")
     ap.add_argument("--json", action="store_true")
     args = ap.parse_args(argv)
     import torch
-    timer = Timer(torch, args.iters, not args.no_flush)
+    timer = Timer(torch, args.iters)
     rows = []
     if args.case in ("projection", "all"):
-        rows += sweep_projection(torch, timer, args.batch or [1, 8, 64, 256], PROJ_SHAPES)
+        shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.shape] if args.shape else PROJ_SHAPES
+        rows += sweep_projection(torch, timer, args.batch or [1, 8, 64, 256], shapes)
     if args.case in ("attention", "all"):
         rows += sweep_attention(torch, timer, args.batch or [1, 64, 256], args.ctx or [1, 128, 1024, 8192, 32768],
                                 args.hd or [64, 96])
