@@ -150,7 +150,8 @@ DeviceModel& LanguageModel::device() const {
 }
 
 void LanguageModel::bind(DecoderState& state) const {
-  if (!state.device || state.device->owner() != &device()) {
+  const DeviceModel& model = device();  // creates the context on first use
+  if (!state.device || state.device->owner() != &model) {
     if (state.position != 0) throw std::invalid_argument("decoder state belongs to another model");
     state.device = std::make_shared<DeviceSequence>(device_, 64);
   }

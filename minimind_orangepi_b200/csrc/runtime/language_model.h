@@ -65,7 +65,7 @@ class LanguageModel {
   void bind(DecoderState& state) const;
 
   MiniMindConfig config_;
-  DenseModelWeights weights_;
+  mutable DenseModelWeights weights_;  // released once uploaded
   std::string weights_bin_;
   RuntimeOptions options_;
   mutable std::shared_ptr<DeviceModel> device_;
