@@ -1,7 +1,7 @@
 // Device helpers shared by the decode kernels (sm_100a only).
 //
 // Everything here is a thin wrapper over one PTX instruction: bulk async copies
-// (cp.async.bulk, never with .multicast), mbarriers, programmatic dependent
+// (cp.async.bulk into this CTA only), mbarriers, programmatic dependent
 // launch controls, ldmatrix / movmatrix / mma.sync fragments.
 #pragma once
 
@@ -82,7 +82,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // Bulk (non-tensor) async copy global -> this CTA's shared memory, completion
 // signalled on `bar` as transaction bytes. dst/src 16-byte aligned, bytes a
-// multiple of 16. No multicast.
+// multiple of 16. Destination is this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
