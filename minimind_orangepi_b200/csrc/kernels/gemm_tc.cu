@@ -28,12 +28,12 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int UM = 128;       // UMMA M (weight rows per CTA)
 constexpr int BK = 64;        // K per stage (one 128-byte swizzle atom of fp16)
-// Stage ring depth per batch tile (about 160 KB of tiles); loads run
-// PD = NSTAGE - 2 tiles ahead, so the stage being refilled belongs to the MMA
-// issued two iterations earlier and the copy never waits on the newest MMA.
+// Stage ring depth per batch tile: at most ~96-144 KB of tiles, so a CTA of
+// this kernel can share an SM with an attention CTA (about 110 KB) when the
+// two halves of a split batch run concurrently.
 template <int BN>
 constexpr int stages_for() {
-  return BN >= 256 ? 4 : (BN >= 128 ? 5 : 8);
+  return BN >= 256 ? 3 : 4;
 }
 
 struct ArgBest {
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
       if (s.seq_pos) s.seq_pos[s.slots[b]] += 1;
       if (s.hist) {
         const int step = *s.hist_step;
-        if (step < s.hist_cap) s.hist[step * a.B + b] = next;
+        if (step < s.hist_cap) s.hist[step * s.hist_stride + b] = next;
       }
     }
   }

@@ -46,6 +46,7 @@ struct TokenSink {
   int* hist = nullptr;            // optional [hist_cap][B] token history
   int* hist_step = nullptr;       // device counter of history rows written
   int hist_cap = 0;
+  int hist_stride = 0;            // elements between history rows
 };
 
 struct ProjArgs {

@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <memory>
@@ -82,6 +83,9 @@ struct mmc_ctx {
   int device = 0;
   int num_sms = 148;
   cudaStream_t stream = nullptr;
+  cudaStream_t stream2 = nullptr;  // second part of a split batch
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  bool split_parts = true;  // run large batches as two concurrent halves
   std::vector<void*> allocs;
 
   // weights
@@ -196,8 +200,12 @@ struct StepIO {
   int* hist = nullptr;
   int* hist_step = nullptr;
   int hist_cap = 0;
+  int hist_stride = 0;  // row stride of the history (the whole graph batch)
   int split_tokens = 64;
   int max_splits = 1;
+  int64_t total_pages = 1, max_ctx = 1;  // attention plan inputs (whole batch)
+  int row0 = 0;  // first scratch row of this part of the batch
+  int part = 0;  // 0/1: which counter region this part uses
 };
 
 // Batches of up to kGemvMaxBatch rows use the CUDA-core projections with
@@ -223,6 +231,20 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   const auto& d = c->d;
   const int H = int(d.hidden_size), I = int(d.intermediate_size), Q = c->q_size(), KV = c->kv_size();
   const int NQKV = Q + 2 * KV;
+  // per-row scratch of this part of the batch (rows row0 .. row0 + B)
+  const size_t r0 = size_t(io.row0);
+  float* const hidden = c->hidden + r0 * H;
+  float* const qkv = c->qkv + r0 * NQKV;
+  float* const attn = c->attn + r0 * Q;
+  float* const act = c->act + r0 * I;
+  __half* const xn16 = c->xn16 + r0 * H;
+  __half* const attn16 = c->attn16 + r0 * Q;
+  __half* const act16 = c->act16 + r0 * I;
+  float* const attn_part = c->attn_part + r0 * size_t(d.num_key_value_heads) * c->max_splits_cap * c->rep() *
+                                                size_t(d.head_dim + 2);
+  unsigned* const attn_counters = c->attn_counters + r0 * size_t(d.num_key_value_heads);
+  void* const argmax_part = static_cast<uint8_t*>(c->argmax_part) + r0 * size_t((d.vocab_size + 127) / 128) * 8;
+  unsigned* const argmax_counter = c->argmax_counter + size_t(io.part) * size_t(c->max_batch + 2);
   const bool tc = io.B > kGemvMaxBatch;
   int evi = 0;
   bool first = true;
@@ -236,11 +258,11 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   };
   auto norm16 = [&](const float* w, bool embed, bool final_norm) {
     mmc::NormArgs n;
-    n.hidden = c->hidden;
-    n.hidden_out = c->hidden;
+    n.hidden = hidden;
+    n.hidden_out = hidden;
     n.w = w;
     n.eps = d.rms_norm_eps;
-    n.out = c->xn16;
+    n.out = xn16;
     n.B = io.B;
     n.H = H;
     n.embed = c->embed;
@@ -270,7 +292,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     // ---- q|k|v projection
     if (tc) {
       norm16(L.in_norm, l == 0, false);
-      tcproj(kKindQkv, mmc::kEpiStore, L.qkv, NQKV, H, c->xn16, c->qkv, nullptr, NQKV);
+      tcproj(kKindQkv, mmc::kEpiStore, L.qkv, NQKV, H, xn16, qkv, nullptr, NQKV);
     } else {
       mmc::ProjArgs p;
       p.B = io.B;
@@ -278,23 +300,23 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
       p.W = L.qkv;
       p.N = NQKV;
       p.K = H;
-      p.in = c->hidden;
+      p.in = hidden;
       p.norm_w = L.in_norm;
       p.eps = d.rms_norm_eps;
-      p.out = c->qkv;
+      p.out = qkv;
       p.ldo = NQKV;
       if (l == 0) {
         p.embed = c->embed;
         p.vocab = int(d.vocab_size);
         p.tokens = io.tokens;
-        p.hidden = c->hidden;
+        p.hidden = hidden;
       }
       const bool pdl = mark(kKindQkv);
       launch_proj(c, l == 0 ? mmc::kProEmbedNorm : mmc::kProNorm, mmc::kEpiStore, p, s, pdl);
     }
     // ---- attention
     mmc::AttnArgs a;
-    a.qkv = c->qkv;
+    a.qkv = qkv;
     a.ld_qkv = NQKV;
     a.q_norm = L.q_norm;
     a.k_norm = L.k_norm;
@@ -315,20 +337,20 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     a.hd = int(d.head_dim);
     a.split_tokens = io.split_tokens;
     a.max_splits = io.max_splits;
-    a.out = tc ? nullptr : c->attn;
-    a.out16 = tc ? c->attn16 : nullptr;
-    a.part = c->attn_part;
-    a.counters = c->attn_counters;
+    a.out = tc ? nullptr : attn;
+    a.out16 = tc ? attn16 : nullptr;
+    a.part = attn_part;
+    a.counters = attn_counters;
     a.err = c->err;
     {
       const bool pdl = mark(kKindAttn);
       ck(mmc::launch_attention(a, s, pdl), "attention launch");
     }
     if (tc) {
-      tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, c->attn16, c->hidden, nullptr, H);
+      tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, attn16, hidden, nullptr, H);
       norm16(L.post_norm, false, false);
-      tcproj(kKindGateUp, mmc::kEpiSwiglu, L.gu, 2 * I, H, c->xn16, nullptr, c->act16, I);
-      tcproj(kKindDown, mmc::kEpiResid, L.down, H, I, c->act16, c->hidden, nullptr, H);
+      tcproj(kKindGateUp, mmc::kEpiSwiglu, L.gu, 2 * I, H, xn16, nullptr, act16, I);
+      tcproj(kKindDown, mmc::kEpiResid, L.down, H, I, act16, hidden, nullptr, H);
       continue;
     }
     // ---- o projection + residual
@@ -338,8 +360,8 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     o.W = L.o;
     o.N = H;
     o.K = Q;
-    o.in = c->attn;
-    o.out = c->hidden;
+    o.in = attn;
+    o.out = hidden;
     o.ldo = H;
     {
       const bool pdl = mark(kKindO);
@@ -352,10 +374,10 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     gu.W = L.gu;
     gu.N = 2 * I;
     gu.K = H;
-    gu.in = c->hidden;
+    gu.in = hidden;
     gu.norm_w = L.post_norm;
     gu.eps = d.rms_norm_eps;
-    gu.out = c->act;
+    gu.out = act;
     gu.ldo = I;
     {
       const bool pdl = mark(kKindGateUp);
@@ -368,8 +390,8 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     dn.W = L.down;
     dn.N = H;
     dn.K = I;
-    dn.in = c->act;
-    dn.out = c->hidden;
+    dn.in = act;
+    dn.out = hidden;
     dn.ldo = H;
     {
       const bool pdl = mark(kKindDown);
@@ -385,17 +407,18 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   sink.hist = io.hist;
   sink.hist_step = io.hist_step;
   sink.hist_cap = io.hist_cap;
+  sink.hist_stride = io.hist_stride > 0 ? io.hist_stride : io.B;
   if (tc) {
     norm16(c->final_norm, false, true);
     mmc::TcArgs t;
     t.W = c->lm_head;
-    t.X = c->xn16;
+    t.X = xn16;
     t.N = int(d.vocab_size);
     t.K = H;
     t.B = io.B;
     t.logits = io.logits;
-    t.argmax_part = c->argmax_part;
-    t.counter = c->argmax_counter;
+    t.argmax_part = argmax_part;
+    t.counter = argmax_counter;
     t.sink = sink;
     t.err = c->err;
     const bool pdl = mark(kKindLm);
@@ -407,17 +430,66 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     lm.W = c->lm_head;
     lm.N = int(d.vocab_size);
     lm.K = H;
-    lm.in = c->hidden;
+    lm.in = hidden;
     lm.norm_w = c->final_norm;
     lm.eps = d.rms_norm_eps;
     lm.logits = io.logits;
-    lm.argmax_part = c->argmax_part;
-    lm.counter = c->argmax_counter;
+    lm.argmax_part = argmax_part;
+    lm.counter = argmax_counter;
     lm.sink = sink;
     const bool pdl = mark(kKindLm);
     launch_proj(c, mmc::kProNormFinal, mmc::kEpiArgmax, lm, s, pdl);
   }
   if (ev) ck(cudaEventRecord(ev[evi++], s), "event record");
+}
+
+// Batches of at least 2 * kSplitMinRows rows on the tensor-core path run as two
+// independent halves on two streams (two parallel branches of the captured
+// graph): sequences never interact, so one half's latency-bound projections
+// overlap the other half's HBM-bound attention.
+constexpr int kSplitMinRows = 32;
+
+bool splits_batch(const mmc_ctx* c, int B) { return c->split_parts && B >= 2 * kSplitMinRows; }
+
+void enqueue_batch(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
+  const int64_t total_pages = io.total_pages, max_ctx = io.max_ctx;
+  if (!splits_batch(c, io.B)) {
+    enqueue_step(c, io, s);
+    return;
+  }
+  const int h = (io.B / 2 + 15) / 16 * 16;
+  StepIO a = io, b = io;
+  a.B = h;
+  b.B = io.B - h;
+  b.row0 = io.row0 + h;
+  b.part = 1;
+  b.slots = io.slots + h;
+  b.tokens = io.tokens + h;
+  if (io.next_out) b.next_out = io.next_out + h;
+  if (io.logits) b.logits = io.logits + size_t(h) * c->d.vocab_size;
+  if (io.hist) b.hist = io.hist + h;
+  if (io.hist_step) b.hist_step = io.hist_step + 1;
+  a.hist_stride = b.hist_stride = io.B;
+  // each half plans its own attention split over about half the pages
+  a.split_tokens = plan_split(c, std::max<int64_t>(1, total_pages * h / io.B), max_ctx, &a.max_splits);
+  b.split_tokens = plan_split(c, std::max<int64_t>(1, total_pages * (io.B - h) / io.B), max_ctx, &b.max_splits);
+  ck(cudaEventRecord(c->fork_ev, s), "fork");
+  ck(cudaStreamWaitEvent(c->stream2, c->fork_ev, 0), "fork");
+  enqueue_step(c, a, s);
+  enqueue_step(c, b, c->stream2);
+  ck(cudaEventRecord(c->join_ev, c->stream2), "join");
+  ck(cudaStreamWaitEvent(s, c->join_ev, 0), "join");
+}
+
+// Positions the captured / planned attention split covers for every part.
+int64_t plan_cap_tokens(const mmc_ctx* c, const StepIO& io) {
+  const int64_t total_pages = io.total_pages, max_ctx = io.max_ctx;
+  if (!splits_batch(c, io.B)) return int64_t(io.max_splits) * io.split_tokens;
+  const int h = (io.B / 2 + 15) / 16 * 16;
+  int ms_a = 1, ms_b = 1;
+  const int sa = plan_split(c, std::max<int64_t>(1, total_pages * h / io.B), max_ctx, &ms_a);
+  const int sb = plan_split(c, std::max<int64_t>(1, total_pages * (io.B - h) / io.B), max_ctx, &ms_b);
+  return std::min(int64_t(ms_a) * sa, int64_t(ms_b) * sb);
 }
 
 void require_ready(const mmc_ctx* c) {
@@ -470,6 +542,8 @@ StepIO plan_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, bool auto_re
   StepIO io;
   io.B = batch;
   io.split_tokens = plan_split(c, total_pages, max_ctx, &io.max_splits);
+  io.total_pages = total_pages;
+  io.max_ctx = max_ctx;
   return io;
 }
 
@@ -630,6 +704,10 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     require(major == 10, MMC_ERR_CUDA, "libminimind_cuda is built for sm_100a (B200) only");
     ck(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device), "device query");
     ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
+    ck(cudaStreamCreateWithFlags(&c->stream2, cudaStreamNonBlocking), "stream");
+    ck(cudaEventCreateWithFlags(&c->fork_ev, cudaEventDisableTiming), "event");
+    ck(cudaEventCreateWithFlags(&c->join_ev, cudaEventDisableTiming), "event");
+    if (const char* e = std::getenv("MMC_SPLIT_BATCH")) c->split_parts = std::atoi(e) != 0;
     ck(mmc::gemv_init_attributes(), "gemv attributes");
     ck(mmc::gemm_tc_init_attributes(), "tensor-core projection attributes");
     ck(mmc::attention_init_attributes(), "attention attributes");
@@ -646,7 +724,11 @@ void mmc_destroy(mmc_ctx* c) {
   drop_graph(c);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->stream2) cudaStreamSynchronize(c->stream2);
   if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->stream2) cudaStreamDestroy(c->stream2);
+  if (c->fork_ev) cudaEventDestroy(c->fork_ev);
+  if (c->join_ev) cudaEventDestroy(c->join_ev);
   delete c;
 }
 
@@ -742,7 +824,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
       part_bytes = std::max(part_bytes, mmc::gemv_argmax_part_bytes(V, H, b, c->num_sms));
     part_bytes = std::max(part_bytes, mmc::tc_argmax_part_bytes(V, max_batch));
     c->argmax_part = c->alloc<uint8_t>(part_bytes, "argmax partials");
-    c->argmax_counter = c->alloc<unsigned>(size_t(max_batch) + 2, "argmax counters");
+    c->argmax_counter = c->alloc<unsigned>(2 * (size_t(max_batch) + 2), "argmax counters (two batch parts)");
     c->attn_part = c->alloc<float>(
         mmc::attn_part_floats(max_batch, int(d.num_key_value_heads), c->max_splits_cap, c->rep(), int(d.head_dim)),
         "attention partials");
@@ -909,7 +991,7 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     if (use_graph) {
       ck(cudaGraphLaunch(c->graph, c->stream), "graph launch");
     } else {
-      enqueue_step(c, io, c->stream);
+      enqueue_batch(c, io, c->stream);
     }
     ck(cudaMemcpyAsync(c->h_stage + 2 * batch, c->tokens, sizeof(int) * batch, cudaMemcpyDeviceToHost, c->stream),
        "D2H next tokens");
@@ -990,7 +1072,7 @@ int mmc_decode_step_async(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, con
     io.tokens = c->tokens;
     io.next_out = d_next;
     io.logits = d_logits;
-    enqueue_step(c, io, s);
+    enqueue_batch(c, io, s);
     for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
   });
 }
@@ -1014,10 +1096,12 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     StepIO io;
     io.B = batch;
     io.split_tokens = plan_split(c, total_pages, cap, &io.max_splits);
+    io.total_pages = total_pages;
+    io.max_ctx = cap;
     if (!c->hist) {
       c->hist_cap = 8192;
       c->hist = c->alloc<int>(size_t(c->hist_cap) * c->max_batch, "token history");
-      c->hist_step = c->alloc<int>(1, "history counter");
+      c->hist_step = c->alloc<int>(2, "history counters (two batch parts)");
     }
     upload(c, c->slots, seq_ids, sizeof(int) * batch, "slots");
     c->async_slots.clear();
@@ -1029,7 +1113,7 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     cudaGraph_t g = nullptr;
     ck(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     try {
-      enqueue_step(c, io, c->stream);
+      enqueue_batch(c, io, c->stream);
     } catch (...) {
       cudaStreamEndCapture(c->stream, &g);
       if (g) cudaGraphDestroy(g);
@@ -1041,7 +1125,7 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     ck(e, "graph instantiate");
     c->graph_batch = batch;
     c->graph_slots.assign(seq_ids, seq_ids + batch);
-    c->graph_cap_tokens = int64_t(io.max_splits) * io.split_tokens;
+    c->graph_cap_tokens = plan_cap_tokens(c, io);
   });
 }
 
@@ -1071,7 +1155,7 @@ int mmc_graph_run(mmc_ctx* c, int32_t n_steps, void* stream) {
               "position exceeds max_position_embeddings");
     }
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    ck(cudaMemsetAsync(c->hist_step, 0, sizeof(int), st), "history reset");
+    ck(cudaMemsetAsync(c->hist_step, 0, 2 * sizeof(int), st), "history reset");
     for (int i = 0; i < n_steps; ++i) ck(cudaGraphLaunch(c->graph, st), "graph launch");
     for (int s : c->graph_slots) c->h_pos[s] += n_steps;
   });
