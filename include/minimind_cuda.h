@@ -173,7 +173,7 @@ MMC_EXPORT int mmc_graph_tokens(mmc_ctx* ctx, int32_t n_steps, int32_t* tokens_h
 /* Wait for the context's stream and report any device-side error. */
 MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
 /* Number of kernels one decode step launches for a batch of `batch` rows
- * (5 per layer + 1 for batch <= 4, 7 per layer + 2 above). */
+ * (6 per layer + 1 for batch <= 4, 8 per layer + 2 above). */
 MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* kernels);
 
 /* ------------------------------------------------------------- single ops

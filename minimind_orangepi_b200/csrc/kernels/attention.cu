@@ -1,38 +1,52 @@
-// Fused decode attention over a paged fp16 KV cache.
+// Fused decode attention over a paged fp16 KV cache: two launches per layer.
 //
 // Replaces, for one decoder layer, the reference's
 //   mini_mind_decode_qkv_postprocess (per-head q/k RMSNorm + RoPE + K/V append,
 //     op_kernel/mini_mind_decode_qkv_postprocess.cpp:54-177; CPU form
-//     decoder_layer.cpp:342-359) and
+//     decoder_layer.cpp:342-359)                          -> qk_prep_kernel
 //   mini_mind_attention (GQA softmax(q.K/sqrt(d)).V over the cache,
 //     op_kernel/mini_mind_attention.cpp:41-91; CPU form decoder_layer.cpp:184-234)
-// with one launch.
+//                                                          -> attention_kernel
 //
-// Grid (split, kv_head, batch_row); 4 warps per CTA. A CTA walks its split of
-// the sequence one 64-token page at a time: each page's K and V slabs (one
-// contiguous 64 x hd fp16 block each) arrive by bulk async copy into a
-// multi-stage shared-memory ring, issued before griddepcontrol.wait because
-// cached positions never depend on the projection kernel in front of it.
-// Each warp owns 16 tokens of a page:
+// qk_prep_kernel (one CTA per batch row and kv head) normalises and rotates the
+// group's q heads into an fp16 buffer and appends the new token's K/V row to
+// the cache page.
+//
+// attention_kernel is persistent (about two CTAs per SM). Work items are
+// (batch row, kv head, split of the context), taken from an atomic queue by a
+// dedicated producer warp that streams each item's 64-position pages -- K and V
+// slabs, one contiguous 64 x hd fp16 block each, plus the item's q heads on its
+// first page -- by bulk async copies into a ring of stages (full/empty
+// mbarriers, per-stage item metadata in shared memory). Four consumer warps
+// take 16 positions of each page:
 //   S^T[16 tok x 8 heads] = K[16 x hd] . Q^T     (mma m16n8k16, heads on N)
 //   online softmax per head (exp2 domain)
 //   P^T -> B fragment by movmatrix (8x8 transpose in registers)
 //   O^T[hd x 8 heads] += V^T[hd x 16 tok] . P^T  (ldmatrix.trans for V^T)
-// The q heads of the GQA group sit on the mma N dimension, so one K/V read
-// serves all of them. Warps, then splits, are merged with the usual
-// (max, sum, acc) rescaling; the last CTA of a (row, kv_head) merges the splits
-// (arrival counter, self-resetting).
+// The GQA group's q heads sit on the mma N dimension, so one K/V read serves
+// all of them. At an item's last page the consumers merge their warps and
+// either write the output or a split partial; the last split to finish a
+// (row, kv head) merges the partials (arrival counter, self-resetting). The
+// producer never waits on the consumers except for a free stage, so copies
+// stay in flight across item boundaries.
 //
 // Rows inside a page are stored with a 16-byte-chunk XOR swizzle (common.cuh
 // swz_chunk) so the flat page copy lands in shared memory already
 // conflict-free for ldmatrix; the append writes the same layout.
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace mmc {
 namespace {
 
-constexpr int kAttnThreads = 128;
+// 4 consumer warps of 16 positions each (8 warps of 8 positions is the other
+// supported split: more page throughput per CTA at long contexts, but slower
+// for the batched decode step at ~1-2 K positions, where two CTAs per SM and
+// the 4-stage ring matter more).
+constexpr int kConsumerWarps = 4;
+constexpr int kTokPerWarp = 64 / kConsumerWarps;
+constexpr int kAttnThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kMaxRep = 8;  // q heads per kv head carried on the mma N dimension
 
 template <int HD>
@@ -43,8 +57,10 @@ struct AttnCfg {
   static constexpr int KC = HD / 16;                     // k-chunks (S) == m-tiles (O)
   static constexpr size_t STAGE_BYTES = size_t(2) * TILE * 2;
   static constexpr size_t RING_BYTES = NST * STAGE_BYTES;
-  static constexpr size_t COMB_FLOATS = 4 * kMaxRep * (HD + 2);
-  static constexpr size_t SMEM = RING_BYTES + COMB_FLOATS * 4 + kMaxRep * HD * 2 + 2 * HD * 2;
+  // per stage: the group's q heads; after the ring: warp partials [warps][rep][HD + 2]
+  __host__ __device__ static size_t q_bytes(int rep) { return size_t(rep) * HD * 2; }
+  __host__ __device__ static size_t comb_floats(int rep) { return size_t(kConsumerWarps) * rep * (HD + 2); }
+  __host__ __device__ static size_t smem(int rep) { return RING_BYTES + NST * q_bytes(rep) + comb_floats(rep) * 4; }
 };
 
 __device__ __forceinline__ size_t page_slab(int page, int layer, int layers, int kv, int nkv, int h, int tile) {
@@ -82,299 +98,435 @@ __device__ __forceinline__ void norm_rope_head(const float* src, const float* w,
   }
 }
 
+struct StageMeta {
+  int b, h, split, tok_begin, tok_end, nch, nsplits, chunk;  // chunk < 0: end of this CTA's stream
+};
+
+// Work item w (split-major numbering). A sequence of P cached pages is cut into
+// n = ceil(P / split_pages) splits of equal size (ceil(P / n) pages), so no
+// split is a short remainder.
+__device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, StageMeta& m) {
+  const int per_split = a.B * a.nkv;
+  m.split = w / per_split;
+  const int bh = w % per_split;
+  m.b = bh / a.nkv;
+  m.h = bh % a.nkv;
+  const int ctx = a.seq_pos[a.slots[m.b]] + 1;
+  const int pages = (ctx + kPageTokens - 1) / kPageTokens;
+  const int split_pages = a.split_tokens / kPageTokens;
+  m.nsplits = (pages + split_pages - 1) / split_pages;
+  if (m.split >= m.nsplits) return false;
+  const int per = (pages + m.nsplits - 1) / m.nsplits;
+  m.tok_begin = m.split * per * kPageTokens;
+  if (m.tok_begin >= ctx) return false;
+  m.tok_end = min(ctx, m.tok_begin + per * kPageTokens);
+  m.nch = (m.tok_end - m.tok_begin + kPageTokens - 1) / kPageTokens;
+  return true;
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
+
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(128) qk_prep_kernel(AttnArgs a) {
   using C = AttnCfg<HD>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  __half* ring = reinterpret_cast<__half*>(smem);
-  float* comb = reinterpret_cast<float*>(smem + C::RING_BYTES);  // [4 warps][8 heads][HD + 2]
-  __half* q_s = reinterpret_cast<__half*>(comb + C::COMB_FLOATS);  // [8][HD]
-  __half* kv_new = q_s + kMaxRep * HD;                             // [2][HD]
-  __shared__ __align__(8) uint64_t bars[C::NST];
-  __shared__ int abort_flag;
-  __shared__ bool is_last;
-
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  __shared__ __align__(16) __half kv_new[2][HD];
+  const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t = lane & 3;
   const int rep = a.nq / a.nkv;
-
-  // Cached positions and the page table were settled before the kernel in
-  // front of this one started (see the file comment), so read them pre-wait.
-  const int slot = a.slots[b];
-  const int pos = a.seq_pos[slot];
-  const int ctx = pos + 1;
-  const int tok_begin = split * a.split_tokens;
-  if (tok_begin >= ctx) {
-    pdl_wait();
-    pdl_launch_dependents();
-    return;
-  }
-  const int tok_end = min(ctx, tok_begin + a.split_tokens);
-  const int nsplits = (ctx + a.split_tokens - 1) / a.split_tokens;
-  const int n_chunks = (tok_end - tok_begin + kPageTokens - 1) / kPageTokens;
-  const bool owns_tail = tok_end == ctx;
-  const int* bt = a.block_table + (size_t)slot * a.max_pages;
-
-  if (tid == 0) {
-    abort_flag = 0;
-    if (pos >= a.max_pos || nsplits > a.max_splits) {
-      set_error(a.err, kDevPositionLimit);
-      abort_flag = 1;
-    }
-    for (int s = 0; s < C::NST; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (abort_flag) {
-    pdl_wait();
-    pdl_launch_dependents();
-    return;
-  }
-
-  auto issue = [&](int c) {  // thread 0 only
-    const int stage = c % C::NST;
-    const int pidx = tok_begin / kPageTokens + c;
-    const int page = pidx < a.max_pages ? bt[pidx] : -1;
-    __half* dst = ring + (size_t)stage * 2 * C::TILE;
-    if (page < 0) {
-      set_error(a.err, kDevNoPage);
-      abort_flag = 1;
-      // complete the phase without data so waiters do not hang
-      mbar_arrive_expect_tx(&bars[stage], 0);
-      return;
-    }
-    mbar_arrive_expect_tx(&bars[stage], uint32_t(C::STAGE_BYTES));
-    bulk_g2s(dst, a.kv_pool + page_slab(page, a.layer, a.layers, 0, a.nkv, h, C::TILE), C::TILE * 2, &bars[stage]);
-    bulk_g2s(dst + C::TILE, a.kv_pool + page_slab(page, a.layer, a.layers, 1, a.nkv, h, C::TILE), C::TILE * 2,
-             &bars[stage]);
-  };
-  if (tid == 0) {
-    for (int c = 0; c < min(C::NST, n_chunks); ++c) issue(c);
-  }
-
   pdl_wait();
   pdl_launch_dependents();
-
-  // ------------------------------------------- q (and tail k/v) post-process
+  const int slot = a.slots[b];
+  const int pos = a.seq_pos[slot];
+  if (pos >= a.max_pos || pos / kPageTokens >= a.max_pages) {
+    if (tid == 0) set_error(a.err, kDevPositionLimit);
+    return;
+  }
   const float* row = a.qkv + (size_t)b * a.ld_qkv;
   const float* cos_r = a.rope_cos + (size_t)pos * (HD / 2);
   const float* sin_r = a.rope_sin + (size_t)pos * (HD / 2);
-  for (int j = warp; j < kMaxRep; j += 4) {
+  for (int j = warp; j < rep + 2; j += 4) {
     if (j < rep) {
-      norm_rope_head<HD>(row + (size_t)(h * rep + j) * HD, a.q_norm, cos_r, sin_r, a.eps, q_s + j * HD, lane);
+      norm_rope_head<HD>(row + (size_t)(h * rep + j) * HD, a.q_norm, cos_r, sin_r, a.eps,
+                         a.q16 + ((size_t)b * a.nq + h * rep + j) * HD, lane);
+    } else if (j == rep) {
+      norm_rope_head<HD>(row + (size_t)(a.nq + h) * HD, a.k_norm, cos_r, sin_r, a.eps, kv_new[0], lane);
     } else {
-      for (int d = lane; d < HD; d += 32) q_s[j * HD + d] = __float2half_rn(0.f);
-    }
-  }
-  const int tail_row = pos % kPageTokens;
-  if (owns_tail) {
-    if (warp == 0) {
-      norm_rope_head<HD>(row + (size_t)(a.nq + h) * HD, a.k_norm, cos_r, sin_r, a.eps, kv_new, lane);
-    } else if (warp == 1) {
       const float* v = row + (size_t)(a.nq + a.nkv + h) * HD;
-      for (int d = lane; d < HD; d += 32) kv_new[HD + d] = __float2half_rn(v[d]);
+      for (int d = lane; d < HD; d += 32) kv_new[1][d] = __float2half_rn(v[d]);
     }
   }
   __syncthreads();
-  if (owns_tail && tid < 2 * C::CPR) {
-    // append the new K/V row into the cache page (swizzled row layout)
+  if (tid < 2 * C::CPR) {
     const int kv = tid / C::CPR, c = tid % C::CPR;
-    const int page = bt[pos / kPageTokens];
-    if (page >= 0) {
-      __half* dst = a.kv_pool + page_slab(page, a.layer, a.layers, kv, a.nkv, h, C::TILE) + (size_t)tail_row * HD +
-                    swz_chunk(tail_row, c, C::CPR) * 8;
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(kv_new + kv * HD + c * 8);
+    const int page = a.block_table[(size_t)slot * a.max_pages + pos / kPageTokens];
+    if (page < 0) {
+      set_error(a.err, kDevNoPage);
+      return;
     }
+    const int r = pos % kPageTokens;
+    __half* dst = a.kv_pool + page_slab(page, a.layer, a.layers, kv, a.nkv, h, C::TILE) + (size_t)r * HD +
+                  swz_chunk(r, c, C::CPR) * 8;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&kv_new[kv][c * 8]);
   }
+}
 
-  // Q^T as the B operand of S^T = K . Q^T: b0 = Q[g][16kc + 2t..], b1 = +8
-  uint32_t qb0[C::KC], qb1[C::KC];
-#pragma unroll
-  for (int kc = 0; kc < C::KC; ++kc) {
-    qb0[kc] = *reinterpret_cast<const uint32_t*>(q_s + g * HD + 16 * kc + 2 * t);
-    qb1[kc] = *reinterpret_cast<const uint32_t*>(q_s + g * HD + 16 * kc + 8 + 2 * t);
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) {
+  using C = AttnCfg<HD>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __half* ring = reinterpret_cast<__half*>(smem);
+  const int rep = a.nq / a.nkv;
+  __half* qring = reinterpret_cast<__half*>(smem + C::RING_BYTES);                        // [NST][rep][HD]
+  float* comb = reinterpret_cast<float*>(smem + C::RING_BYTES + C::NST * C::q_bytes(rep));  // [warps][rep][HD+2]
+  __shared__ __align__(8) uint64_t full_bar[C::NST];
+  __shared__ __align__(8) uint64_t empty_bar[C::NST];
+  __shared__ StageMeta meta[C::NST];
+  __shared__ bool is_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int total_items = a.max_splits * a.B * a.nkv;
+
+  if (tid == 0) {
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kConsumerWarps);
+    }
+    fence_mbar_init();
   }
+  __syncthreads();
+  // q heads and the appended rows come from qk_prep_kernel just before this
+  pdl_wait();
+  pdl_launch_dependents();
 
-  const float sl2 = 1.4426950408889634f / sqrtf(float(HD));
-  float mA = -1e30f, mB = -1e30f, lA = 0.f, lB = 0.f;
-  float o[C::KC][4];
-#pragma unroll
-  for (int mt = 0; mt < C::KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-
-  const int r0 = warp * 16;
-  for (int c = 0; c < n_chunks; ++c) {
-    const int stage = c % C::NST;
-    const uint32_t parity = (c / C::NST) & 1;
-    if (!mbar_wait_bounded(&bars[stage], parity, a.err)) abort_flag = 1;
-    __half* kt = ring + (size_t)stage * 2 * C::TILE;
-    __half* vt = kt + C::TILE;
-    const bool tail_chunk = owns_tail && c == n_chunks - 1;
-    if (tail_chunk) {
-      __syncthreads();
-      if (tid < 2 * C::CPR) {
-        const int kv = tid / C::CPR, cc = tid % C::CPR;
-        __half* dst = (kv ? vt : kt) + tail_row * HD + swz_chunk(tail_row, cc, C::CPR) * 8;
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(kv_new + kv * HD + cc * 8);
+  if (warp == kConsumerWarps) {
+    // ======================================================= producer warp
+    // The whole warp runs the producer: lane 0 issues the copies, all lanes
+    // hold 32 page-table entries of the current item (one load round trip
+    // per 32 pages), and the next work item is taken from the queue and
+    // decoded right after the current item's first page is issued, while the
+    // ring is full -- so item boundaries cost the consumers nothing.
+    auto fetch = [&](StageMeta& m) -> bool {  // warp-uniform
+      while (true) {
+        int w = 0;
+        if (lane == 0) w = int(atomicAdd(&a.work[0], 1u));
+        w = __shfl_sync(0xffffffffu, w, 0);
+        if (w >= total_items) return false;
+        if (!decode_item(a, w, m)) continue;
+        if (m.nsplits > a.max_splits) {
+          if (lane == 0) set_error(a.err, kDevPositionLimit);
+          continue;
+        }
+        return true;
+      }
+    };
+    auto load_pages = [&](const StageMeta& m, int block) {  // entries [block*32, block*32+32) of the item
+      const int pidx = m.tok_begin / kPageTokens + block * 32 + lane;
+      const int slot = a.slots[m.b];
+      return (block * 32 + lane < m.nch && pidx < a.max_pages) ? a.block_table[(size_t)slot * a.max_pages + pidx]
+                                                              : -1;
+    };
+    StageMeta cur{}, nxt{};
+    bool have_cur = fetch(cur), have_nxt = false, nxt_decoded = false;
+    int cur_pages = have_cur ? load_pages(cur, 0) : -1, nxt_pages = -1;
+    int chunk = 0;
+    bool done = !have_cur;
+    for (int c = 0;; ++c) {
+      const int s = c % C::NST;
+      if (c >= C::NST) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait_bounded(&empty_bar[s], ((c / C::NST) - 1) & 1, a.err);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) done = true;
+      }
+      if (!done && chunk >= cur.nch) {  // current item exhausted: move to the next
+        if (!nxt_decoded) {
+          have_nxt = fetch(nxt);
+          nxt_pages = have_nxt ? load_pages(nxt, 0) : -1;
+        }
+        nxt_decoded = false;
+        if (!have_nxt) {
+          done = true;
+        } else {
+          cur = nxt;
+          cur_pages = nxt_pages;
+          chunk = 0;
+        }
+      }
+      int page = -1;
+      if (!done) {
+        if (chunk > 0 && (chunk & 31) == 0) cur_pages = load_pages(cur, chunk >> 5);
+        page = __shfl_sync(0xffffffffu, cur_pages, chunk & 31);
+        if (page < 0) {
+          if (lane == 0) set_error(a.err, kDevNoPage);
+          done = true;
+        }
+      }
+      if (done) {
+        if (lane == 0) {
+          meta[s].chunk = -1;
+          mbar_arrive_expect_tx(&full_bar[s], 0);
+        }
+        break;
+      }
+      if (lane == 0) {
+        StageMeta m = cur;
+        m.chunk = chunk;
+        meta[s] = m;
+        const bool first = chunk == 0;
+        const uint32_t qbytes = uint32_t(rep * HD * 2);
+        mbar_arrive_expect_tx(&full_bar[s], uint32_t(C::STAGE_BYTES) + (first ? qbytes : 0u));
+        __half* dst = ring + (size_t)s * 2 * C::TILE;
+        bulk_g2s(dst, a.kv_pool + page_slab(page, a.layer, a.layers, 0, a.nkv, cur.h, C::TILE), C::TILE * 2,
+                 &full_bar[s]);
+        bulk_g2s(dst + C::TILE, a.kv_pool + page_slab(page, a.layer, a.layers, 1, a.nkv, cur.h, C::TILE),
+                 C::TILE * 2, &full_bar[s]);
+        if (first)
+          bulk_g2s(qring + (size_t)s * rep * HD, a.q16 + ((size_t)cur.b * a.nq + cur.h * rep) * HD, qbytes,
+                   &full_bar[s]);
+      }
+      __syncwarp();
+      ++chunk;
+      if (chunk == 1 && !nxt_decoded) {  // ring is full: look ahead to the next item now
+        have_nxt = fetch(nxt);
+        nxt_pages = have_nxt ? load_pages(nxt, 0) : -1;
+        nxt_decoded = true;
       }
     }
-    __syncthreads();
-    if (abort_flag) return;
-
-    const int tok0 = tok_begin + c * kPageTokens + r0;
-    if (tok0 < tok_end) {
-      // ---- S^T = K . Q^T over this warp's 16 tokens
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
+    __syncwarp();
+  } else {
+    // ====================================================== consumer warps
+    const int g = lane >> 2, t = lane & 3;
+    const float sl2 = 1.4426950408889634f / sqrtf(float(HD));
+    const int r0 = warp * kTokPerWarp;
+    const size_t pstride = (size_t)rep * (HD + 2);
+    StageMeta it{};
+    uint32_t qb0[C::KC], qb1[C::KC];
+    float mA = -1e30f, mB = -1e30f, lA = 0.f, lB = 0.f;
+    float o[C::KC][4];
+    for (int c = 0;; ++c) {
+      const int s = c % C::NST;
+      if (!mbar_wait_bounded(&full_bar[s], (c / C::NST) & 1, a.err)) break;
+      const StageMeta m = meta[s];
+      if (m.chunk < 0) break;
+      const __half* kt = ring + (size_t)s * 2 * C::TILE;
+      const __half* vt = kt + C::TILE;
+      if (m.chunk == 0) {  // a new item: its q heads arrived with this page
+        it = m;
+        const __half* qs = qring + (size_t)s * rep * HD;
 #pragma unroll
-      for (int kc = 0; kc < C::KC; ++kc) {
-        const int rr = r0 + ((lane >> 3) & 1) * 8 + (lane & 7);
-        const int ch = 2 * kc + (lane >> 4);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(smem_u32(kt + rr * HD + swz_chunk(rr, ch, C::CPR) * 8), a0, a1, a2, a3);
-        mma16816(s, a0, a1, a2, a3, qb0[kc], qb1[kc]);
+        for (int kc = 0; kc < C::KC; ++kc) {
+          qb0[kc] = g < rep ? *reinterpret_cast<const uint32_t*>(qs + g * HD + 16 * kc + 2 * t) : 0u;
+          qb1[kc] = g < rep ? *reinterpret_cast<const uint32_t*>(qs + g * HD + 16 * kc + 8 + 2 * t) : 0u;
+        }
+        mA = mB = -1e30f;
+        lA = lB = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < C::KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
       }
-      const bool v0 = tok0 + g < tok_end, v1 = tok0 + g + 8 < tok_end;
-      const float sA0 = v0 ? s[0] * sl2 : -INFINITY, sB0 = v0 ? s[1] * sl2 : -INFINITY;
-      const float sA1 = v1 ? s[2] * sl2 : -INFINITY, sB1 = v1 ? s[3] * sl2 : -INFINITY;
-      float mxA = fmaxf(sA0, sA1), mxB = fmaxf(sB0, sB1);
+      const int tok0 = it.tok_begin + m.chunk * kPageTokens + r0;
+      if (tok0 < it.tok_end) {
+        // ---- S^T = K . Q^T over this warp's positions (rows 8-15 of the
+        //      m16 tile repeat rows 0-7 when a warp owns 8 positions; masked)
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kc = 0; kc < C::KC; ++kc) {
+          const int rr = r0 + (kTokPerWarp == 16 ? ((lane >> 3) & 1) * 8 : 0) + (lane & 7);
+          const int chn = 2 * kc + (lane >> 4);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(smem_u32(kt + rr * HD + swz_chunk(rr, chn, C::CPR) * 8), a0, a1, a2, a3);
+          mma16816(sc, a0, a1, a2, a3, qb0[kc], qb1[kc]);
+        }
+        const bool v0 = tok0 + g < it.tok_end, v1 = kTokPerWarp == 16 && tok0 + g + 8 < it.tok_end;
+        const float sA0 = v0 ? sc[0] * sl2 : -INFINITY, sB0 = v0 ? sc[1] * sl2 : -INFINITY;
+        const float sA1 = v1 ? sc[2] * sl2 : -INFINITY, sB1 = v1 ? sc[3] * sl2 : -INFINITY;
+        float mxA = fmaxf(sA0, sA1), mxB = fmaxf(sB0, sB1);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, off));
+          mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, off));
+        }
+        const float nA = fmaxf(mA, mxA), nB = fmaxf(mB, mxB);
+        const float alA = exp2f(mA - nA), alB = exp2f(mB - nB);
+        mA = nA;
+        mB = nB;
+        const float pA0 = exp2f(sA0 - nA), pB0 = exp2f(sB0 - nB);
+        const float pA1 = exp2f(sA1 - nA), pB1 = exp2f(sB1 - nB);
+        lA = lA * alA + pA0 + pA1;
+        lB = lB * alB + pB0 + pB1;
+#pragma unroll
+        for (int mt = 0; mt < C::KC; ++mt) {
+          o[mt][0] *= alA;
+          o[mt][1] *= alB;
+          o[mt][2] *= alA;
+          o[mt][3] *= alB;
+        }
+        // ---- P^T as the B operand: transpose the two 8x8 halves in registers
+        const uint32_t pb0 = movmatrix_t(pack_half2(pA0, pB0));
+        const uint32_t pb1 = movmatrix_t(pack_half2(pA1, pB1));
+        // ---- O^T += V^T . P^T
+#pragma unroll
+        for (int mt = 0; mt < C::KC; ++mt) {
+          const int rr = r0 + (kTokPerWarp == 16 ? ((lane >> 4) & 1) * 8 : 0) + (lane & 7);
+          const int chn = 2 * mt + ((lane >> 3) & 1);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(smem_u32(vt + rr * HD + swz_chunk(rr, chn, C::CPR) * 8), a0, a1, a2, a3);
+          mma16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);  // this warp is done with the stage
+      if (m.chunk != it.nch - 1) continue;
+
+      // ---------------------------------------------- item done: merge warps
+      float lAr = lA, lBr = lB;
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
-        mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, off));
-        mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, off));
+        lAr += __shfl_xor_sync(0xffffffffu, lAr, off);
+        lBr += __shfl_xor_sync(0xffffffffu, lBr, off);
       }
-      const float nA = fmaxf(mA, mxA), nB = fmaxf(mB, mxB);
-      const float alA = exp2f(mA - nA), alB = exp2f(mB - nB);
-      mA = nA;
-      mB = nB;
-      const float pA0 = exp2f(sA0 - nA), pB0 = exp2f(sB0 - nB);
-      const float pA1 = exp2f(sA1 - nA), pB1 = exp2f(sB1 - nB);
-      lA = lA * alA + pA0 + pA1;
-      lB = lB * alB + pB0 + pB1;
+      {
+        float* cw = comb + (size_t)warp * rep * (HD + 2);
+        const int hA = 2 * t, hB = 2 * t + 1;
+        if (hA < rep) {
 #pragma unroll
-      for (int mt = 0; mt < C::KC; ++mt) {
-        o[mt][0] *= alA;
-        o[mt][1] *= alB;
-        o[mt][2] *= alA;
-        o[mt][3] *= alB;
-      }
-      // ---- P^T as the B operand: transpose the two 8x8 halves in registers
-      const uint32_t pb0 = movmatrix_t(pack_half2(pA0, pB0));
-      const uint32_t pb1 = movmatrix_t(pack_half2(pA1, pB1));
-      // ---- O^T += V^T . P^T
+          for (int mt = 0; mt < C::KC; ++mt) {
+            cw[hA * (HD + 2) + 16 * mt + g] = o[mt][0];
+            cw[hA * (HD + 2) + 16 * mt + g + 8] = o[mt][2];
+          }
+          if (g == 0) {
+            cw[hA * (HD + 2) + HD] = mA;
+            cw[hA * (HD + 2) + HD + 1] = lAr;
+          }
+        }
+        if (hB < rep) {
 #pragma unroll
-      for (int mt = 0; mt < C::KC; ++mt) {
-        const int rr = r0 + ((lane >> 4) & 1) * 8 + (lane & 7);
-        const int ch = 2 * mt + ((lane >> 3) & 1);
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_t(smem_u32(vt + rr * HD + swz_chunk(rr, ch, C::CPR) * 8), a0, a1, a2, a3);
-        mma16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+          for (int mt = 0; mt < C::KC; ++mt) {
+            cw[hB * (HD + 2) + 16 * mt + g] = o[mt][1];
+            cw[hB * (HD + 2) + 16 * mt + g + 8] = o[mt][3];
+          }
+          if (g == 0) {
+            cw[hB * (HD + 2) + HD] = mB;
+            cw[hB * (HD + 2) + HD + 1] = lBr;
+          }
+        }
       }
-    }
-    __syncthreads();  // every warp is done with this stage
-    if (tid == 0 && c + C::NST < n_chunks) {
-      fence_proxy_async_smem();
-      issue(c + C::NST);
+      consumer_sync();
+      float* part_bh = a.part + ((size_t)it.b * a.nkv + it.h) * a.max_splits * pstride;
+      const size_t out_off = (size_t)it.b * a.nq * HD + (size_t)it.h * rep * HD;
+      auto put_out = [&](int idx, float v) {
+        if (a.out16) a.out16[out_off + idx] = __float2half_rn(v);
+        else a.out[out_off + idx] = v;
+      };
+      for (int i = tid; i < rep * HD; i += kConsumerWarps * 32) {
+        const int j = i / HD, d = i % HD;
+        float M = -1e30f;
+        for (int w4 = 0; w4 < kConsumerWarps; ++w4) M = fmaxf(M, comb[(w4 * rep + j) * (HD + 2) + HD]);
+        float L = 0.f, O = 0.f;
+        for (int w4 = 0; w4 < kConsumerWarps; ++w4) {
+          const float* cw = comb + (w4 * rep + j) * (HD + 2);
+          const float f = exp2f(cw[HD] - M);
+          L += cw[HD + 1] * f;
+          O += cw[d] * f;
+        }
+        if (it.nsplits == 1) {
+          put_out(j * HD + d, O / L);
+        } else {
+          float* pp = part_bh + it.split * pstride + j * (HD + 2);
+          pp[d] = O;
+          if (d == 0) {
+            pp[HD] = M;
+            pp[HD + 1] = L;
+          }
+        }
+      }
+      if (it.nsplits > 1) {
+        // ------------------------------------ merge splits (last arrival)
+        // The barrier orders every consumer's partial stores before thread 0's
+        // acquire-release arrival (release is cumulative); the last arrival's
+        // acquire plus the next barrier order the merge's loads after them.
+        consumer_sync();
+        if (tid == 0)
+          is_last = atom_add_acq_rel_gpu(&a.counters[(size_t)it.b * a.nkv + it.h], 1u) == unsigned(it.nsplits - 1);
+        consumer_sync();
+        if (is_last) {
+          // stage the split partials in shared memory (comb is free now) with
+          // independent coalesced loads, then merge from there
+          const int n = it.nsplits * int(pstride);
+          const bool staged = n <= int(C::comb_floats(rep));
+          if (staged) {
+            for (int i = tid; i < n; i += kConsumerWarps * 32) comb[i] = __ldcg(part_bh + i);
+            consumer_sync();
+          }
+          const float* src = staged ? comb : part_bh;
+          for (int i = tid; i < rep * HD; i += kConsumerWarps * 32) {
+            const int j = i / HD, d = i % HD;
+            float M = -1e30f;
+            for (int sp = 0; sp < it.nsplits; ++sp) M = fmaxf(M, src[sp * pstride + j * (HD + 2) + HD]);
+            float L = 0.f, O = 0.f;
+            for (int sp = 0; sp < it.nsplits; ++sp) {
+              const float* pp = src + sp * pstride + j * (HD + 2);
+              const float f = exp2f(pp[HD] - M);
+              L += pp[HD + 1] * f;
+              O += pp[d] * f;
+            }
+            put_out(j * HD + d, O / L);
+          }
+          if (tid == 0) a.counters[(size_t)it.b * a.nkv + it.h] = 0u;
+        }
+      }
+      consumer_sync();  // comb is reused by the next item
     }
   }
 
-  // ------------------------------------------------- merge the 4 warps
-#pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    lA += __shfl_xor_sync(0xffffffffu, lA, off);
-    lB += __shfl_xor_sync(0xffffffffu, lB, off);
-  }
-  {
-    float* cw = comb + (size_t)warp * kMaxRep * (HD + 2);
-    const int hA = 2 * t, hB = 2 * t + 1;
-#pragma unroll
-    for (int mt = 0; mt < C::KC; ++mt) {
-      cw[hA * (HD + 2) + 16 * mt + g] = o[mt][0];
-      cw[hB * (HD + 2) + 16 * mt + g] = o[mt][1];
-      cw[hA * (HD + 2) + 16 * mt + g + 8] = o[mt][2];
-      cw[hB * (HD + 2) + 16 * mt + g + 8] = o[mt][3];
-    }
-    if (g == 0) {
-      cw[hA * (HD + 2) + HD] = mA;
-      cw[hA * (HD + 2) + HD + 1] = lA;
-      cw[hB * (HD + 2) + HD] = mB;
-      cw[hB * (HD + 2) + HD + 1] = lB;
-    }
-  }
+  // ---- queue reset: the last CTA to leave clears the work counters
   __syncthreads();
-
-  const size_t pstride = (size_t)rep * (HD + 2);
-  float* part_bh = a.part + ((size_t)b * a.nkv + h) * a.max_splits * pstride;
-  const size_t out_off = (size_t)b * a.nq * HD + (size_t)h * rep * HD;
-  auto put_out = [&](int idx, float v) {
-    if (a.out16) a.out16[out_off + idx] = __float2half_rn(v);
-    else a.out[out_off + idx] = v;
-  };
-  for (int i = tid; i < rep * HD; i += kAttnThreads) {
-    const int j = i / HD, d = i % HD;
-    float M = -1e30f;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, comb[(w * kMaxRep + j) * (HD + 2) + HD]);
-    float L = 0.f, O = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      const float* cw = comb + (w * kMaxRep + j) * (HD + 2);
-      const float f = exp2f(cw[HD] - M);
-      L += cw[HD + 1] * f;
-      O += cw[d] * f;
-    }
-    if (nsplits == 1) {
-      put_out(j * HD + d, O / L);
-    } else {
-      float* p = part_bh + split * pstride + j * (HD + 2);
-      p[d] = O;
-      if (d == 0) {
-        p[HD] = M;
-        p[HD + 1] = L;
-      }
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(&a.work[1], 1u) == gridDim.x - 1) {
+      a.work[0] = 0u;
+      a.work[1] = 0u;
     }
   }
-  if (nsplits == 1) return;
-
-  // ---------------------------------------------- merge splits (last CTA)
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(&a.counters[(size_t)b * a.nkv + h], 1u) == unsigned(nsplits - 1);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int i = tid; i < rep * HD; i += kAttnThreads) {
-    const int j = i / HD, d = i % HD;
-    float M = -1e30f;
-    for (int s = 0; s < nsplits; ++s) M = fmaxf(M, __ldcg(part_bh + s * pstride + j * (HD + 2) + HD));
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < nsplits; ++s) {
-      const float* p = part_bh + s * pstride + j * (HD + 2);
-      const float f = exp2f(__ldcg(p + HD) - M);
-      L += __ldcg(p + HD + 1) * f;
-      O += __ldcg(p + d) * f;
-    }
-    put_out(j * HD + d, O / L);
-  }
-  if (tid == 0) a.counters[(size_t)b * a.nkv + h] = 0u;
 }
 
 template <int HD>
 cudaError_t launch_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.max_splits, a.nkv, a.B);
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = AttnCfg<HD>::SMEM;
-  cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t prep = {};
+  prep.gridDim = dim3(a.nkv, a.B);
+  prep.blockDim = dim3(128);
+  prep.stream = s;
+  prep.attrs = attr;
+  prep.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&prep, qk_prep_kernel<HD>, a);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  const int items = a.max_splits * a.nkv * a.B;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int per_sm = a.ctas_per_sm > 0 ? a.ctas_per_sm : 2;
+  cfg.gridDim = dim3(items < per_sm * sms ? items : per_sm * sms);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = AttnCfg<HD>::smem(a.nq / a.nkv);
+  cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = 1;  // always overlaps qk_prep_kernel's tail
   return cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
 }
 
 template <int HD>
 cudaError_t attr_hd() {
   return cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(AttnCfg<HD>::SMEM));
+                              int(AttnCfg<HD>::smem(kMaxRep)));
 }
 
 }  // namespace
@@ -395,7 +547,7 @@ cudaError_t attention_init_attributes() {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   if (a.nkv <= 0 || a.nq % a.nkv != 0 || a.nq / a.nkv > kMaxRep || a.split_tokens % kPageTokens != 0 ||
-      a.max_splits <= 0 || a.B <= 0)
+      a.max_splits <= 0 || a.B <= 0 || a.work == nullptr || a.q16 == nullptr)
     return cudaErrorInvalidValue;
   switch (a.hd) {
     case 16: return launch_hd<16>(a, s, pdl);

@@ -117,9 +117,9 @@ struct NormArgs {
 };
 cudaError_t launch_rmsnorm_f16(const NormArgs& a, bool embed, bool final_norm, cudaStream_t stream, bool pdl);
 
-// Fused decode attention: q/k per-head RMSNorm + rotate-half RoPE, K/V append
-// into the paged cache, split-KV GQA flash-decode over the cache, split
-// combine. One launch per layer.
+// Fused decode attention: q/k per-head RMSNorm + rotate-half RoPE and K/V
+// append into the paged cache (prep launch), then split-KV GQA flash-decode
+// over the cache with split combine (persistent launch). Two launches per layer.
 struct AttnArgs {
   const float* qkv = nullptr;  // [B][(nq + 2 nkv) * hd] raw projections (fp32)
   int ld_qkv = 0;
@@ -142,6 +142,9 @@ struct AttnArgs {
   __half* out16 = nullptr;  // [B][nq * hd] fp16 when set (tensor-core path)
   float* part = nullptr;  // [B][nkv][max_splits][rep][hd + 2] split partials
   unsigned* counters = nullptr;  // [B][nkv], zero-initialised, self-resetting
+  unsigned* work = nullptr;      // [2] work-queue head and exit count, zero-initialised, self-resetting
+  __half* q16 = nullptr;         // [B][nq][hd] fp16 normalised + rotated q (written by the prep launch)
+  int ctas_per_sm = 0;           // persistent grid size per SM (0: 2)
   int* err = nullptr;
 };
 constexpr int kPageTokens = 64;

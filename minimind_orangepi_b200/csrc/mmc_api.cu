@@ -2,7 +2,7 @@
 // behind the C ABI declared in include/minimind_cuda.h.
 //
 // One decode step for B rows is a fixed chain of kernels on one stream
-// (5 per layer + 1), every launch after the first carrying programmatic
+// (6 per layer + 1; 8 + 2 on the tensor-core path), every launch after the first carrying programmatic
 // stream serialization so each kernel's weight / KV-page prefetch overlaps its
 // predecessor:
 //   per layer: qkv projection (RMSNorm prologue; layer 0 gathers the embedding)
@@ -112,11 +112,13 @@ struct mmc_ctx {
   // per-step scratch (sized for max_batch)
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
   __half *xn16 = nullptr, *attn16 = nullptr, *act16 = nullptr;  // tensor-core path activations
+  __half* q16 = nullptr;  // normalised + rotated q heads, [max_batch][nq][hd]
   int *tokens = nullptr, *slots = nullptr, *next = nullptr;
   void* argmax_part = nullptr;
   unsigned* argmax_counter = nullptr;
   float* attn_part = nullptr;
   unsigned* attn_counters = nullptr;
+  unsigned* attn_work = nullptr;  // [2 parts][2] attention work-queue words
   int* err = nullptr;
   int* h_stage = nullptr;  // pinned: [2][max_batch] ints
   int max_splits_cap = 64;
@@ -179,7 +181,14 @@ void check_device_error(mmc_ctx* c) {
 // times over, at most `max_splits_cap` splits per sequence.
 int plan_split_raw(int64_t total_pages, int64_t nkv, int num_sms, int cap, int64_t max_ctx, int* max_splits) {
   const int64_t pages = std::max<int64_t>(1, (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens);
-  int64_t sp = std::max<int64_t>(1, total_pages * nkv / (4 * num_sms));
+  // work items per persistent attention CTA (2 per SM): enough that the
+  // queue's tail is short, few enough that per-item merging stays cheap
+  static const int items_per_cta = [] {
+    const char* e = std::getenv("MMC_ATTN_ITEMS_PER_CTA");
+    const int v = e ? std::atoi(e) : 1;
+    return v > 0 ? v : 1;
+  }();
+  int64_t sp = std::max<int64_t>(1, total_pages * nkv / (int64_t(items_per_cta) * 2 * num_sms));
   sp = std::max<int64_t>(sp, (pages + cap - 1) / cap);
   sp = std::min<int64_t>(sp, pages);
   *max_splits = int((pages + sp - 1) / sp);
@@ -204,19 +213,20 @@ struct StepIO {
   int split_tokens = 64;
   int max_splits = 1;
   int64_t total_pages = 1, max_ctx = 1;  // attention plan inputs (whole batch)
+  int attn_ctas_per_sm = 2;  // persistent attention CTAs per SM (1 when two halves share the GPU)
   int row0 = 0;  // first scratch row of this part of the batch
   int part = 0;  // 0/1: which counter region this part uses
 };
 
 // Batches of up to kGemvMaxBatch rows use the CUDA-core projections with
-// fused RMSNorm prologues (5 kernels per layer); larger batches the tensor-core
-// projections behind an fp16 RMSNorm kernel (7 per layer).
+// fused RMSNorm prologues (6 kernels per layer); larger batches the tensor-core
+// projections behind an fp16 RMSNorm kernel (8 per layer).
 constexpr int kGemvMaxBatch = 4;
 enum Kind { kKindQkv = 0, kKindAttn = 1, kKindO = 2, kKindGateUp = 3, kKindDown = 4, kKindLm = 5, kKindNorm = 6 };
 
 int kernels_per_step(const mmc_ctx* c, int B) {
   const int L = int(c->d.num_hidden_layers);
-  return B <= kGemvMaxBatch ? 5 * L + 1 : 7 * L + 2;
+  return B <= kGemvMaxBatch ? 6 * L + 1 : 8 * L + 2;  // attention is two launches
 }
 
 void launch_proj(mmc_ctx* c, int pro, int epi, const mmc::ProjArgs& a, cudaStream_t s, bool pdl) {
@@ -341,6 +351,9 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     a.out16 = tc ? attn16 : nullptr;
     a.part = attn_part;
     a.counters = attn_counters;
+    a.work = c->attn_work + 2 * io.part;
+    a.q16 = c->q16 + r0 * Q;
+    a.ctas_per_sm = io.attn_ctas_per_sm;
     a.err = c->err;
     {
       const bool pdl = mark(kKindAttn);
@@ -449,6 +462,15 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
 // overlap the other half's HBM-bound attention.
 constexpr int kSplitMinRows = 32;
 
+int attn_ctas_split() {
+  static const int v = [] {
+    const char* e = std::getenv("MMC_ATTN_CTAS_SPLIT");
+    const int x = e ? std::atoi(e) : 1;
+    return x > 0 ? x : 1;
+  }();
+  return v;
+}
+
 bool splits_batch(const mmc_ctx* c, int B) { return c->split_parts && B >= 2 * kSplitMinRows; }
 
 void enqueue_batch(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
@@ -470,6 +492,7 @@ void enqueue_batch(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
   if (io.hist) b.hist = io.hist + h;
   if (io.hist_step) b.hist_step = io.hist_step + 1;
   a.hist_stride = b.hist_stride = io.B;
+  a.attn_ctas_per_sm = b.attn_ctas_per_sm = attn_ctas_split();
   // each half plans its own attention split over about half the pages
   a.split_tokens = plan_split(c, std::max<int64_t>(1, total_pages * h / io.B), max_ctx, &a.max_splits);
   b.split_tokens = plan_split(c, std::max<int64_t>(1, total_pages * (io.B - h) / io.B), max_ctx, &b.max_splits);
@@ -815,6 +838,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->xn16 = c->alloc<__half>(size_t(max_batch) * H, "normed activations");
     c->attn16 = c->alloc<__half>(size_t(max_batch) * Q, "attention output fp16");
     c->act16 = c->alloc<__half>(size_t(max_batch) * I, "act fp16");
+    c->q16 = c->alloc<__half>(size_t(max_batch) * Q, "q fp16");
     c->logits = c->alloc<float>(size_t(max_batch) * V, "logits");
     c->tokens = c->alloc<int>(size_t(max_batch), "tokens");
     c->slots = c->alloc<int>(size_t(max_batch), "slots");
@@ -829,6 +853,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
         mmc::attn_part_floats(max_batch, int(d.num_key_value_heads), c->max_splits_cap, c->rep(), int(d.head_dim)),
         "attention partials");
     c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
+    c->attn_work = c->alloc<unsigned>(4, "attention work queue");
     ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
     ck(cudaDeviceSynchronize(), "KV init");
     c->kv_ready = true;
@@ -1036,7 +1061,7 @@ int mmc_profile_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const in
         kind_ms[k] = 0.f;
         kind_launches[k] = 0;
       }
-      for (int i = 0; i < n; ++i) {
+      for (int i = 0; i < int(kinds.size()); ++i) {
         float ms = 0.f;
         ck(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]), "event time");
         const int kind = kinds[size_t(i)];
@@ -1306,8 +1331,9 @@ int mmc_op_attention_workspace_size(int32_t batch, int32_t nq, int32_t nkv, int3
     require(batch >= 1 && nkv >= 1 && nq % nkv == 0 && hd > 0 && max_ctx >= 1 && bytes, MMC_ERR_INVALID,
             "bad arguments");
     const int splits = std::min(64, (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens);
+    // split partials | counters, error word, work queue | q heads (fp16)
     *bytes = (mmc::attn_part_floats(batch, nkv, splits, nq / nkv, hd) * 4 + 255) / 256 * 256 +
-             size_t(batch) * nkv * 4 + 256;
+             (size_t(batch) * nkv * 4 + 32 + 255) / 256 * 256 + size_t(batch) * nq * hd * 2;
   });
 }
 
@@ -1356,8 +1382,10 @@ int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t
     a.part = reinterpret_cast<float*>(base);
     a.counters = reinterpret_cast<unsigned*>(base + pbytes);
     a.err = reinterpret_cast<int*>(base + pbytes + size_t(batch) * nkv * 4);
+    a.work = reinterpret_cast<unsigned*>(base + pbytes + size_t(batch) * nkv * 4 + 16);
+    a.q16 = reinterpret_cast<__half*>(base + pbytes + (size_t(batch) * nkv * 4 + 32 + 255) / 256 * 256);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    ck(cudaMemsetAsync(base + pbytes, 0, size_t(batch) * nkv * 4 + 4, s), "counter reset");
+    ck(cudaMemsetAsync(base + pbytes, 0, size_t(batch) * nkv * 4 + 32, s), "counter reset");
     ck(mmc::launch_attention(a, s, false), "attention launch");
   });
 }
