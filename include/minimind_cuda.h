@@ -147,9 +147,10 @@ MMC_EXPORT int mmc_decode_step(mmc_ctx* ctx, int32_t batch, const int32_t* seq_i
 
 /* One decode step like mmc_decode_step, with a CUDA event between every two
  * kernels (programmatic overlap off) so each kernel's device time is
- * measured. kind_ms[6] / kind_launches[6] receive the summed milliseconds and
- * launch counts per kernel kind: 0 qkv projection, 1 attention, 2 o
- * projection, 3 gate/up projection, 4 down projection, 5 lm_head + argmax. */
+ * measured. kind_ms[7] / kind_launches[7] receive the summed milliseconds and
+ * launch counts per kernel kind: 0 qkv projection, 1 attention (q/k prep +
+ * attention), 2 o projection, 3 gate/up projection, 4 down projection,
+ * 5 lm_head + argmax, 6 embedding gather (batches above 4). */
 MMC_EXPORT int mmc_profile_step(mmc_ctx* ctx, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
                                 int32_t* next_tokens, float* kind_ms, int32_t* kind_launches);
 

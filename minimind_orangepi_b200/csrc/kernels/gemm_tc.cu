@@ -17,8 +17,22 @@
 //                    lanes 32w..32w+31 = weight rows) fused with the store /
 //                    residual add / SiLU*mul / argmax of the decode step.
 //
+// RMSNorm is carried across kernels instead of run as its own pass: the norm
+// weight is folded into the consuming projection's W at load time, a residual
+// epilogue writes the fp16 residual rows plus one sum of squares per (row,
+// M-tile), and the consumer scales its outputs by 1/rms (computed by the
+// otherwise idle warps 2-3 during the K loop).
+//
+// Split-K (projections with fewer tiles than SMs): the k-splits of one tile
+// run as a thread-block cluster; each parks its accumulator in its stage ring
+// and the ranks reduce disjoint column slices over distributed shared memory
+// in rank order, so results do not depend on scheduling.
+//
 // Every wait is bounded (2 s): on timeout the kernel records an error, frees
 // its TMEM and returns.
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -71,6 +85,31 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+template <int BN>
+__device__ __forceinline__ void tmem_dealloc(uint32_t tmem) {
+  tc_fence_after();
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(BN < 32 ? 32 : BN))
+               : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cta address -> the same offset in cluster CTA `rank`'s shared memory
+__device__ __forceinline__ uint32_t map_dsmem(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
@@ -104,12 +143,17 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
   __shared__ __align__(8) uint64_t done_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
-  __shared__ ArgBest best_s[4][BN];
+  __shared__ ArgBest best_s[EPI == kEpiArgmax ? 4 : 1][BN];
+  __shared__ float rs_s[BN];
+  __shared__ float ssw_s[EPI == kEpiResid ? 4 : 1][BN];
   __shared__ bool is_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int m0 = blockIdx.x * UM, n0 = blockIdx.y * BN;
-  const int KT = a.K / BK;
+  // split-K: blockIdx.z takes k-steps [kbase, kbase + KT) of the K / 64 total
+  const int KT_all = a.K / BK, S = gridDim.z, kz = blockIdx.z;
+  const int kbase = int((long long)kz * KT_all / S);
+  const int KT = int((long long)(kz + 1) * KT_all / S) - kbase;
   const int pre = KT < NSTAGE ? KT : NSTAGE;
 
   if (tid == 0) {
@@ -123,7 +167,7 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
     // weight tiles do not depend on the previous kernel: start them now
     for (int s = 0; s < pre; ++s) {
       mbar_arrive_expect_tx(&full_bar[s], uint32_t(ST_BYTES));
-      tma_load_2d(smem + s * ST_BYTES, &a.map_w, s * BK, m0, &full_bar[s]);
+      tma_load_2d(smem + s * ST_BYTES, &a.map_w, (kbase + s) * BK, m0, &full_bar[s]);
     }
   }
   __syncthreads();
@@ -142,7 +186,8 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
-      for (int s = 0; s < pre; ++s) tma_load_2d(smem + s * ST_BYTES + A_BYTES, &a.map_x, s * BK, n0, &full_bar[s]);
+      for (int s = 0; s < pre; ++s)
+        tma_load_2d(smem + s * ST_BYTES + A_BYTES, &a.map_x, (kbase + s) * BK, n0, &full_bar[s]);
       for (int kt = pre; kt < KT; ++kt) {
         const int s = kt % NSTAGE;
         if (!mbar_wait_bounded(&empty_bar[s], ((kt / NSTAGE) - 1) & 1, a.err)) {
@@ -150,8 +195,8 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
           break;
         }
         mbar_arrive_expect_tx(&full_bar[s], uint32_t(ST_BYTES));
-        tma_load_2d(smem + s * ST_BYTES, &a.map_w, kt * BK, m0, &full_bar[s]);
-        tma_load_2d(smem + s * ST_BYTES + A_BYTES, &a.map_x, kt * BK, n0, &full_bar[s]);
+        tma_load_2d(smem + s * ST_BYTES, &a.map_w, (kbase + kt) * BK, m0, &full_bar[s]);
+        tma_load_2d(smem + s * ST_BYTES + A_BYTES, &a.map_x, (kbase + kt) * BK, n0, &full_bar[s]);
       }
     }
     __syncwarp();
@@ -175,74 +220,168 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
       umma_commit(&done_bar);  // arrives once every MMA above has completed
     }
     __syncwarp();
+  } else {
+    // warps 2-3, idle during the K loop: the folded RMSNorm's per-column
+    // 1/rms of the input (sums of squares from the producer of X) and the
+    // zeroed per-warp sums of squares of a residual epilogue
+    const int t = tid - 64;
+    if (a.ss_in != nullptr) {
+      const int parts = (a.K + UM - 1) / UM;
+      for (int c = t; c < BN; c += 64) {
+        float r = 1.f;
+        if (n0 + c < a.B) {
+          float ss = 0.f;
+          for (int m = 0; m < parts; ++m) ss += a.ss_in[size_t(n0 + c) * parts + m];
+          r = 1.0f / sqrtf(ss / float(a.K) + a.eps);
+        }
+        rs_s[c] = r;
+      }
+    }
+    if (EPI == kEpiResid)
+      for (int c = t; c < 4 * BN; c += 64) (&ssw_s[0][0])[c] = 0.f;
   }
   if (!mbar_wait_bounded(&done_bar, 0, a.err)) abort_flag = 1;
   tc_fence_after();
   __syncthreads();
 
-  ArgBest bst[BN / 16 > 0 ? BN / 16 : 1];
-  if (!abort_flag) {
-    const int row = m0 + warp * 32 + lane;  // this thread's weight row
-    const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
-#pragma unroll 1
-    for (int cc = 0; cc < BN; cc += 16) {
-      float v[16];
-      tmem_ld16(trow + cc, v);
-      if (EPI == kEpiStore || EPI == kEpiResid) {
-        if (row < a.N) {
+  const int row = m0 + warp * 32 + lane;  // this thread's weight row
+  const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
+
+  const bool want_ss = EPI == kEpiResid && a.ss_out != nullptr;
+
+  // Epilogue of NC batch columns c0 .. c0 + NC (values v of this thread's
+  // row); all lanes of the warp take part. Global loads are issued for all
+  // columns before any cross-lane reduction.
+  auto epi_cols = [&](int c0, int nc, float* v) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int b = n0 + cc + j;
-            if (b < a.B) {
-              float* o = a.out + size_t(b) * a.ldo + row;
-              if (EPI == kEpiResid) *o += v[j];
-              else *o = v[j];
-            }
-          }
-        }
-      } else if (EPI == kEpiSwiglu) {
-        // gate rows 16j..16j+7 and up rows 16j+8..16j+15 sit 8 lanes apart
+    for (int j = 0; j < 16; ++j)
+      if (a.ss_in != nullptr && j < nc) v[j] *= rs_s[c0 + j];
+    if (EPI == kEpiStore) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float up = __shfl_down_sync(0xffffffffu, v[j], 8);
-          const int b = n0 + cc + j;
-          if ((lane & 8) == 0 && row < a.N && b < a.B) {
-            const float g = v[j];
-            const int i = (row >> 4) * 8 + (row & 7);
-            a.out16[size_t(b) * a.ldo + i] = __float2half_rn((g / (1.0f + expf(-g))) * up);
-          }
-        }
-      } else {  // argmax over this CTA's rows, per batch column
+      for (int j = 0; j < 16; ++j) {
+        const int b = n0 + c0 + j;
+        if (j < nc && row < a.N && b < a.B) a.out[size_t(b) * a.ldo + row] = v[j];
+      }
+    } else if (EPI == kEpiResid) {
+      float nv[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int b = n0 + cc + j;
-          if (a.logits && row < a.N && b < a.B) a.logits[size_t(b) * a.N + row] = v[j];
-          float bv = row < a.N ? v[j] : -INFINITY;
-          int bi = row < a.N ? row : 0x7fffffff;
+      for (int j = 0; j < 16; ++j) {
+        const int b = n0 + c0 + j;
+        nv[j] = (j < nc && row < a.N && b < a.B) ? a.out[size_t(b) * a.ldo + row] : 0.f;
+      }
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (better(ov, oi, bv, bi)) {
-              bv = ov;
-              bi = oi;
-            }
-          }
-          if (lane == 0) best_s[warp][cc + j] = {bv, bi};
+      for (int j = 0; j < 16; ++j) {
+        const int b = n0 + c0 + j;
+        if (j < nc && row < a.N && b < a.B) {
+          nv[j] += v[j];
+          a.out[size_t(b) * a.ldo + row] = nv[j];
+          if (a.h16_out) a.h16_out[size_t(b) * a.N + row] = __float2half_rn(nv[j]);
         }
       }
+      if (want_ss) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (j < nc) {
+            const float sq = warp_sum(nv[j] * nv[j]);
+            if (lane == 0) ssw_s[warp][c0 + j] = sq;
+          }
+        }
+      }
+    } else if (EPI == kEpiSwiglu) {
+      // gate rows 16j..16j+7 and up rows 16j+8..16j+15 sit 8 lanes apart
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= nc) continue;
+        const float up = __shfl_down_sync(0xffffffffu, v[j], 8);
+        const int b = n0 + c0 + j;
+        if ((lane & 8) == 0 && row < a.N && b < a.B) {
+          const float g = v[j];
+          const int i = (row >> 4) * 8 + (row & 7);
+          a.out16[size_t(b) * a.ldo + i] = __float2half_rn((g / (1.0f + expf(-g))) * up);
+        }
+      }
+    } else {  // argmax over this CTA's rows, per batch column
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (j >= nc) continue;
+        const int b = n0 + c0 + j;
+        if (a.logits && row < a.N && b < a.B) a.logits[size_t(b) * a.N + row] = v[j];
+        float bv = row < a.N ? v[j] : -INFINITY;
+        int bi = row < a.N ? row : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0) best_s[warp][c0 + j] = {bv, bi};
+      }
     }
+  };
+
+  int c_lo = 0, c_hi = BN;  // batch columns this CTA finishes
+  if (S == 1) {
+    if (!abort_flag) {
+#pragma unroll 1
+      for (int cc = 0; cc < BN; cc += 16) {
+        float v[16];
+        tmem_ld16(trow + cc, v);
+        epi_cols(cc, 16, v);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc<BN>(tmem);
+  } else {
+    // split-K cluster: every CTA parks its fp32 accumulator in its (now idle)
+    // stage ring as [column][row]; CTA rank r then sums column slice r over
+    // all ranks in rank order through distributed shared memory.
+    float* red = reinterpret_cast<float*>(smem);
+    if (!abort_flag) {
+#pragma unroll 1
+      for (int cc = 0; cc < BN; cc += 16) {
+        float v[16];
+        tmem_ld16(trow + cc, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) red[(cc + j) * UM + warp * 32 + lane] = v[j];
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc<BN>(tmem);
+    cluster_sync();
+    const int rank = int(cluster_ctarank());
+    c_lo = rank * BN / S;
+    c_hi = (rank + 1) * BN / S;
+    if (!abort_flag) {
+      const uint32_t local = smem_u32(red) + uint32_t(warp * 32 + lane) * 4u;
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+        const int nc = c_hi - c0 < 16 ? c_hi - c0 : 16;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        for (int q = 0; q < S; ++q) {
+          const uint32_t peer = map_dsmem(local + uint32_t(c0 * UM) * 4u, uint32_t(q));
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (j < nc) v[j] += ld_dsmem_f32(peer + uint32_t(j * UM) * 4u);
+        }
+        epi_cols(c0, nc, v);
+      }
+    }
+    cluster_sync();  // peers' rings stay alive until every rank has read them
   }
-  (void)bst;
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(uint32_t(BN < 32 ? 32 : BN))
-                 : "memory");
+  if (abort_flag) return;
+  if (want_ss) {
+    __syncthreads();
+    for (int c = c_lo + tid; c < c_hi; c += kThreads)
+      if (n0 + c < a.B)
+        a.ss_out[size_t(n0 + c) * gridDim.x + blockIdx.x] = ssw_s[0][c] + ssw_s[1][c] + ssw_s[2][c] + ssw_s[3][c];
   }
-  if (EPI != kEpiArgmax || abort_flag) return;
+  if (EPI != kEpiArgmax) return;
 
   ArgBest* part = reinterpret_cast<ArgBest*>(a.argmax_part);
   if (tid < BN && n0 + tid < a.B) {
@@ -298,47 +437,40 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
   }
 }
 
-// RMSNorm of each batch row to fp16 (the tensor-core projections' input).
-// kEmbed: row = embed[token[b]], also written to hidden[b] (layer 0).
-template <bool kEmbed, bool kFinal>
-__global__ void __launch_bounds__(256) rmsnorm_f16_kernel(NormArgs a) {
+// Layer-0 rows of the tensor-core path: embedding gather into the residual
+// stream and its fp16 copy, plus the row's sum of squares for the folded
+// RMSNorm of the first projection (slot 0; the other M-tile slots are 0).
+__global__ void __launch_bounds__(256) embed_rows_kernel(EmbedArgs a) {
   __shared__ float red[8];
   const int b = blockIdx.x, tid = threadIdx.x;
   pdl_wait();
   pdl_launch_dependents();
-  const float* src = a.hidden + size_t(b) * a.H;
-  float* const hidden_w = a.hidden_out;
-  if (kEmbed) {
-    int tok = a.tokens[b];
-    if (tok < 0 || tok >= a.vocab) {
-      set_error(a.err, kDevBadToken);
-      tok = 0;
-    }
-    src = a.embed + size_t(tok) * a.H;
+  int tok = a.tokens[b];
+  if (tok < 0 || tok >= a.vocab) {
+    set_error(a.err, kDevBadToken);
+    tok = 0;
   }
+  const float* src = a.embed + size_t(tok) * a.H;
   float ss = 0.f;
   for (int k = tid * 4; k < a.H; k += 1024) {
     const float4 v = *reinterpret_cast<const float4*>(src + k);
-    if (kEmbed) *reinterpret_cast<float4*>(hidden_w + size_t(b) * a.H + k) = v;
+    *reinterpret_cast<float4*>(a.hidden + size_t(b) * a.H + k) = v;
+    uint2 h;
+    h.x = pack_half2(v.x, v.y);
+    h.y = pack_half2(v.z, v.w);
+    *reinterpret_cast<uint2*>(a.h16 + size_t(b) * a.H + k) = h;
     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   ss = warp_sum(ss);
   if ((tid & 31) == 0) red[tid >> 5] = ss;
   __syncthreads();
-  float tot = 0.f;
+  const int parts = (a.H + UM - 1) / UM;
+  if (tid < parts) {
+    float tot = 0.f;
+    if (tid == 0)
 #pragma unroll
-  for (int w = 0; w < 8; ++w) tot += red[w];
-  const float rs = 1.0f / sqrtf(tot / float(a.H) + a.eps);
-  for (int k = tid * 4; k < a.H; k += 1024) {
-    const float4 v = *reinterpret_cast<const float4*>(src + k);
-    const float4 w = *reinterpret_cast<const float4*>(a.w + k);
-    float4 o;
-    if (kFinal) o = make_float4((v.x * rs) * w.x, (v.y * rs) * w.y, (v.z * rs) * w.z, (v.w * rs) * w.w);
-    else o = make_float4(v.x * (rs * w.x), v.y * (rs * w.y), v.z * (rs * w.z), v.w * (rs * w.w));
-    uint2 h;
-    h.x = pack_half2(o.x, o.y);
-    h.y = pack_half2(o.z, o.w);
-    *reinterpret_cast<uint2*>(a.out + size_t(b) * a.H + k) = h;
+      for (int w = 0; w < 8; ++w) tot += red[w];
+    a.ss[size_t(b) * parts + tid] = tot;
   }
 }
 
@@ -350,15 +482,26 @@ constexpr size_t tc_smem() {
 template <int BN, int EPI>
 cudaError_t launch_bn(const TcArgs& a, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + UM - 1) / UM, (a.B + BN - 1) / BN);
+  cfg.gridDim = dim3((a.N + UM - 1) / UM, (a.B + BN - 1) / BN, a.splits > 1 ? a.splits : 1);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = tc_smem<BN>();
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (a.splits > 1) {  // the k-splits of one tile form a cluster
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = unsigned(a.splits);
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI>, a);
 }
 
@@ -393,10 +536,37 @@ cudaError_t make_map(CUtensorMap* m, const __half* base, int rows, int K, int bo
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return v && *v ? std::atoi(v) : dflt;
+}
+
+// Split-K plan for projections whose (M-tile x batch-tile) grid leaves SMs
+// idle: a batch tile of up to 32 rows and enough k-splits (each at least two
+// 64-wide k-steps, at most 8: one portable cluster) to reach about one CTA
+// per SM. Returns the split count (1: no split) and sets *bn.
+int split_plan(const TcArgs& a, int epi, int* bn) {
+  *bn = tc_batch_tile(a.N, a.B);
+  static const int enabled = env_int("MMC_TC_SPLIT", 1);
+  static const int target = env_int("MMC_TC_SPLIT_TARGET", 148);
+  static const int bn_cap = env_int("MMC_TC_SPLIT_BN", 32);
+  if (!enabled || epi == kEpiArgmax || a.max_splits < 2) return 1;
+  const int mt = (a.N + UM - 1) / UM, KT = a.K / BK;
+  if (mt * ((a.B + *bn - 1) / *bn) >= target || KT < 4) return 1;
+  int b = 16;
+  while (b < bn_cap && b < a.B) b *= 2;
+  const int tiles = mt * ((a.B + b - 1) / b);
+  const int S = std::min(std::min(KT / 2, std::min(a.max_splits, 8)), (target + tiles - 1) / tiles);
+  if (S < 2) return 1;
+  *bn = b;
+  return S;
+}
+
 template <int EPI>
 cudaError_t launch_epi(const TcArgs& a_in, cudaStream_t s, bool pdl) {
-  const int bn = tc_batch_tile(a_in.N, a_in.B);
   TcArgs a = a_in;
+  int bn = 16;
+  a.splits = split_plan(a_in, EPI, &bn);
   cudaError_t e = make_map(&a.map_w, a.W, a.N, a.K, UM);
   if (e != cudaSuccess) return e;
   e = make_map(&a.map_x, a.X, a.B, a.K, bn);
@@ -431,6 +601,11 @@ cudaError_t attrs_bn() {
 
 }  // namespace
 
+int tc_split_k(const TcArgs& a, int epi) {
+  int bn;
+  return split_plan(a, epi, &bn);
+}
+
 // Batch tile: the largest of {256,128,64,32} that still gives every SM work,
 // else 32 (small problems are latency-bound; more CTAs help).
 int tc_batch_tile(int N, int B) {
@@ -463,8 +638,8 @@ cudaError_t launch_gemm_tc(int epi, const TcArgs& a, cudaStream_t s, bool pdl) {
   }
 }
 
-cudaError_t launch_rmsnorm_f16(const NormArgs& a, bool embed, bool final_norm, cudaStream_t s, bool pdl) {
-  if (a.H % 4 != 0 || a.B < 1) return cudaErrorInvalidValue;
+cudaError_t launch_embed_rows(const EmbedArgs& a, cudaStream_t s, bool pdl) {
+  if (a.H % 4 != 0 || a.B < 1 || (a.H + UM - 1) / UM > 256) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.B);
   cfg.blockDim = dim3(256);
@@ -474,9 +649,7 @@ cudaError_t launch_rmsnorm_f16(const NormArgs& a, bool embed, bool final_norm, c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (embed) return cudaLaunchKernelEx(&cfg, rmsnorm_f16_kernel<true, false>, a);
-  if (final_norm) return cudaLaunchKernelEx(&cfg, rmsnorm_f16_kernel<false, true>, a);
-  return cudaLaunchKernelEx(&cfg, rmsnorm_f16_kernel<false, false>, a);
+  return cudaLaunchKernelEx(&cfg, embed_rows_kernel, a);
 }
 
 }  // namespace mmc

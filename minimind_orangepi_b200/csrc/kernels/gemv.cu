@@ -124,10 +124,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(ProjArgs a, int rows_per
     for (int b = 0; b < B; ++b) {
       float* xb = x_s + b * K;
       const float r = rs[b];
-      for (int k = tid; k < K; k += kThreads) {
-        if (PRO == kProNormFinal) xb[k] = (xb[k] * r) * a.norm_w[k];
-        else xb[k] = xb[k] * (r * a.norm_w[k]);
-      }
+      // the norm weight is folded into W's columns at load time
+      for (int k = tid; k < K; k += kThreads) xb[k] *= r;
     }
   }
   __syncthreads();

@@ -23,8 +23,8 @@ enum DeviceError : int {
 // Prologue: how a projection kernel builds its input rows x[b][0..K).
 enum Prologue : int {
   kProPlain = 0,      // x = in[b]                              (fp32 activations)
-  kProNorm = 1,       // x = in[b] * (rs * w)                   decoder_layer.cpp:32-42
-  kProNormFinal = 2,  // x = (in[b] * rs) * w                   language_model.cpp:24-38
+  kProNorm = 1,       // x = in[b] * rs (w folded into W)       decoder_layer.cpp:32-42
+  kProNormFinal = 2,  // final norm, same form                  language_model.cpp:24-38
   kProEmbedNorm = 3,  // in[b] = embed[token[b]] (also written to `hidden`), then kProNorm
 };
 
@@ -54,8 +54,7 @@ struct ProjArgs {
   int N = 0, K = 0, B = 0;
   // prologue
   const float* in = nullptr;  // [B][K] fp32 (hidden / activations)
-  const float* norm_w = nullptr;
-  float eps = 0.f;
+  float eps = 0.f;  // RMSNorm prologues (x * rs; the norm weight is folded into W)
   const float* embed = nullptr;  // [vocab][K] fp32
   int vocab = 0;
   const int* tokens = nullptr;
@@ -95,27 +94,44 @@ struct TcArgs {
   unsigned* counter = nullptr;   // kEpiArgmax: tc_counter_words zeroed words
   TokenSink sink;
   int* err = nullptr;
+  // split-K: gridDim.z = splits CTAs of one tile form a thread-block cluster
+  // and reduce their accumulators over distributed shared memory (fixed order)
+  int splits = 1;      // set by the launcher
+  int max_splits = 8;  // caller's cap (1: never split)
+  // RMSNorm folded across kernels (the norm weight is folded into W's
+  // columns at load time): a consumer with ss_in scales its outputs by
+  // rs[b] = 1 / sqrt(sum_m ss_in[b][m] / K + eps), m < ceil(K / 128); a
+  // kEpiResid producer writes the fp16 copy of the updated residual rows
+  // (h16_out, [B][N]) and its per-M-tile sums of squares
+  // (ss_out[b][blockIdx.x], stride ceil(N / 128)).
+  const float* ss_in = nullptr;
+  float eps = 0.f;
+  __half* h16_out = nullptr;
+  float* ss_out = nullptr;
 };
 int tc_batch_tile(int N, int B);
+// split-K factor the launcher uses for this projection (1 = none)
+// (environment overrides MMC_TC_SPLIT, MMC_TC_SPLIT_BN, MMC_TC_SPLIT_TARGET)
+int tc_split_k(const TcArgs& a, int epi);
 size_t tc_argmax_part_bytes(int N, int B);
 int tc_counter_words(int N, int B);
 cudaError_t launch_gemm_tc(int epi, const TcArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t gemm_tc_init_attributes();
 
-// RMSNorm of B rows to fp16 (input of the tensor-core projections).
-struct NormArgs {
-  const float* hidden = nullptr;  // [B][H] residual stream (written from embed when embedding)
-  float* hidden_out = nullptr;
-  const float* w = nullptr;
-  float eps = 0.f;
-  __half* out = nullptr;  // [B][H]
-  int B = 0, H = 0;
-  const float* embed = nullptr;
+// Layer-0 input of the tensor-core path: gathers embedding rows into the
+// residual stream, its fp16 copy and the sums of squares the first
+// projection's folded RMSNorm needs.
+struct EmbedArgs {
+  const float* embed = nullptr;  // [vocab][H]
   const int* tokens = nullptr;
   int vocab = 0;
+  float* hidden = nullptr;   // [B][H]
+  __half* h16 = nullptr;     // [B][H]
+  float* ss = nullptr;       // [B][ceil(H / 128)]: slot 0 = sum of squares, others 0
+  int B = 0, H = 0;
   int* err = nullptr;
 };
-cudaError_t launch_rmsnorm_f16(const NormArgs& a, bool embed, bool final_norm, cudaStream_t stream, bool pdl);
+cudaError_t launch_embed_rows(const EmbedArgs& a, cudaStream_t stream, bool pdl);
 
 // Fused decode attention: q/k per-head RMSNorm + rotate-half RoPE and K/V
 // append into the paged cache (prep launch), then split-KV GQA flash-decode
@@ -154,11 +170,13 @@ cudaError_t attention_init_attributes();
 
 // Weight packing: fp32 source rows -> fp16 destination rows (RNE), with an
 // optional gate/up interleave by blocks of 8 rows.
-cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s);
+// col_scale (optional, [cols]): folded RMSNorm weight, W[n][k] * col_scale[k]
+cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s,
+                             const float* col_scale = nullptr);
 cudaError_t launch_hold(uint64_t ns, cudaStream_t s);
 cudaError_t launch_fill_kv(__half* pool, const int* pages, int n_tokens, int64_t page_halves, int row_halves,
                            uint32_t seed, cudaStream_t s);
 cudaError_t launch_pack_gate_up(const float* gate, const float* up, __half* dst, int64_t inter, int64_t cols,
-                                cudaStream_t s);
+                                cudaStream_t s, const float* col_scale = nullptr);
 
 }  // namespace mmc

@@ -10,25 +10,33 @@
 // but interleaved in blocks of 8 rows: packed rows [16j, 16j+8) are gate rows
 // [8j, 8j+8) and packed rows [16j+8, 16j+16) the matching up rows, so the
 // SiLU*mul epilogue finds gate_i and up_i 8 rows apart inside one 16-row tile.
+//
+// A projection that reads an RMSNorm output gets the norm weight folded into
+// its columns (W'[n][k] = W[n][k] * w[k], rounded once): the decode kernels then
+// only scale by the per-row 1/rms, which lets the tensor-core path carry the
+// norm across kernels without a normalisation pass.
 #include "kernels.h"
 
 namespace mmc {
 namespace {
 
-__global__ void pack_rows_kernel(const float* __restrict__ src, __half* __restrict__ dst, int64_t n) {
+__global__ void pack_rows_kernel(const float* __restrict__ src, __half* __restrict__ dst, int64_t n, int64_t cols,
+                                 const float* __restrict__ col_scale) {
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
-    dst[i] = __float2half_rn(src[i]);
+    dst[i] = __float2half_rn(col_scale ? src[i] * col_scale[i % cols] : src[i]);
 }
 
 __global__ void pack_gate_up_kernel(const float* __restrict__ gate, const float* __restrict__ up,
-                                    __half* __restrict__ dst, int64_t inter, int64_t cols) {
+                                    __half* __restrict__ dst, int64_t inter, int64_t cols,
+                                    const float* __restrict__ col_scale) {
   const int64_t n = 2 * inter * cols;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t prow = i / cols, c = i % cols;
     const int64_t blk = prow / 16, r = prow % 16;
     const int64_t src_row = blk * 8 + (r & 7);
     const float* s = r < 8 ? gate : up;
-    dst[i] = __float2half_rn(s[src_row * cols + c]);
+    const float v = s[src_row * cols + c];
+    dst[i] = __float2half_rn(col_scale ? v * col_scale[c] : v);
   }
 }
 
@@ -80,15 +88,16 @@ cudaError_t launch_fill_kv(__half* pool, const int* pages, int n_tokens, int64_t
   return cudaGetLastError();
 }
 
-cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s) {
-  pack_rows_kernel<<<1184, 256, 0, s>>>(src, dst, rows * cols);
+cudaError_t launch_pack_rows(const float* src, __half* dst, int64_t rows, int64_t cols, cudaStream_t s,
+                             const float* col_scale) {
+  pack_rows_kernel<<<1184, 256, 0, s>>>(src, dst, rows * cols, cols, col_scale);
   return cudaGetLastError();
 }
 
 cudaError_t launch_pack_gate_up(const float* gate, const float* up, __half* dst, int64_t inter, int64_t cols,
-                                cudaStream_t s) {
+                                cudaStream_t s, const float* col_scale) {
   if (inter % 8 != 0) return cudaErrorInvalidValue;
-  pack_gate_up_kernel<<<1184, 256, 0, s>>>(gate, up, dst, inter, cols);
+  pack_gate_up_kernel<<<1184, 256, 0, s>>>(gate, up, dst, inter, cols, col_scale);
   return cudaGetLastError();
 }
 

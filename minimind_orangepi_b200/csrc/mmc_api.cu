@@ -71,6 +71,11 @@ T* dalloc(size_t count, const char* what) {
   return static_cast<T*>(p);
 }
 
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return v && *v ? std::atoi(v) : dflt;
+}
+
 struct Layer {
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   __half *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
@@ -111,7 +116,7 @@ struct mmc_ctx {
 
   // per-step scratch (sized for max_batch)
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
-  __half *xn16 = nullptr, *attn16 = nullptr, *act16 = nullptr;  // tensor-core path activations
+  __half *h16 = nullptr, *attn16 = nullptr, *act16 = nullptr;  // tensor-core path activations
   __half* q16 = nullptr;  // normalised + rotated q heads, [max_batch][nq][hd]
   int *tokens = nullptr, *slots = nullptr, *next = nullptr;
   void* argmax_part = nullptr;
@@ -119,6 +124,8 @@ struct mmc_ctx {
   float* attn_part = nullptr;
   unsigned* attn_counters = nullptr;
   unsigned* attn_work = nullptr;  // [2 parts][2] attention work-queue words
+  int decode_split_k = env_int("MMC_DECODE_SPLIT_K", 1);
+  float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
   int* err = nullptr;
   int* h_stage = nullptr;  // pinned: [2][max_batch] ints
   int max_splits_cap = 64;
@@ -226,7 +233,9 @@ enum Kind { kKindQkv = 0, kKindAttn = 1, kKindO = 2, kKindGateUp = 3, kKindDown 
 
 int kernels_per_step(const mmc_ctx* c, int B) {
   const int L = int(c->d.num_hidden_layers);
-  return B <= kGemvMaxBatch ? 6 * L + 1 : 8 * L + 2;  // attention is two launches
+  // attention is two launches; the tensor-core path adds the layer-0
+  // embedding gather (its RMSNorms are folded into the projections)
+  return B <= kGemvMaxBatch ? 6 * L + 1 : 6 * L + 2;
 }
 
 void launch_proj(mmc_ctx* c, int pro, int epi, const mmc::ProjArgs& a, cudaStream_t s, bool pdl) {
@@ -247,7 +256,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   float* const qkv = c->qkv + r0 * NQKV;
   float* const attn = c->attn + r0 * Q;
   float* const act = c->act + r0 * I;
-  __half* const xn16 = c->xn16 + r0 * H;
+  __half* const h16 = c->h16 + r0 * H;
   __half* const attn16 = c->attn16 + r0 * Q;
   __half* const act16 = c->act16 + r0 * I;
   float* const attn_part = c->attn_part + r0 * size_t(d.num_key_value_heads) * c->max_splits_cap * c->rep() *
@@ -266,25 +275,40 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     first = false;
     return pdl;
   };
-  auto norm16 = [&](const float* w, bool embed, bool final_norm) {
-    mmc::NormArgs n;
-    n.hidden = hidden;
-    n.hidden_out = hidden;
-    n.w = w;
-    n.eps = d.rms_norm_eps;
-    n.out = xn16;
-    n.B = io.B;
-    n.H = H;
-    n.embed = c->embed;
-    n.tokens = io.tokens;
-    n.vocab = int(d.vocab_size);
-    n.err = c->err;
+  // tensor-core path: h16 holds the fp16 residual rows, ss their per-M-tile
+  // sums of squares; each RMSNorm is the norm weight folded into the next
+  // projection's W and a 1/rms scale in its epilogue.
+  float* const ss = c->ss + r0 * size_t((H + 127) / 128);
+  auto embed_rows = [&] {
+    mmc::EmbedArgs e;
+    e.embed = c->embed;
+    e.tokens = io.tokens;
+    e.vocab = int(d.vocab_size);
+    e.hidden = hidden;
+    e.h16 = h16;
+    e.ss = ss;
+    e.B = io.B;
+    e.H = H;
+    e.err = c->err;
     const bool pdl = mark(kKindNorm);
-    ck(mmc::launch_rmsnorm_f16(n, embed, final_norm, s, pdl), "rmsnorm launch");
+    ck(mmc::launch_embed_rows(e, s, pdl), "embedding launch");
   };
+  // normed: the input is the residual stream (scale by 1/rms); resid: update
+  // the residual stream and emit its fp16 copy and sums of squares
   auto tcproj = [&](Kind k, int epi, const __half* W, int N, int K, const __half* X, float* out, __half* out16,
-                    int ldo) {
+                    int ldo, bool normed) {
     mmc::TcArgs t;
+    // split-K clusters lose to plain tiles inside the decode step (measured on
+    // B200 with the two concurrent batch halves); MMC_DECODE_SPLIT_K=n allows n
+    t.max_splits = c->decode_split_k;
+    if (normed) {
+      t.ss_in = ss;
+      t.eps = d.rms_norm_eps;
+    }
+    if (epi == mmc::kEpiResid) {
+      t.h16_out = h16;
+      t.ss_out = ss;
+    }
     t.W = W;
     t.X = X;
     t.N = N;
@@ -301,8 +325,8 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     const Layer& L = c->layers[l];
     // ---- q|k|v projection
     if (tc) {
-      norm16(L.in_norm, l == 0, false);
-      tcproj(kKindQkv, mmc::kEpiStore, L.qkv, NQKV, H, xn16, qkv, nullptr, NQKV);
+      if (l == 0) embed_rows();
+      tcproj(kKindQkv, mmc::kEpiStore, L.qkv, NQKV, H, h16, qkv, nullptr, NQKV, true);
     } else {
       mmc::ProjArgs p;
       p.B = io.B;
@@ -311,7 +335,6 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
       p.N = NQKV;
       p.K = H;
       p.in = hidden;
-      p.norm_w = L.in_norm;
       p.eps = d.rms_norm_eps;
       p.out = qkv;
       p.ldo = NQKV;
@@ -360,10 +383,9 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
       ck(mmc::launch_attention(a, s, pdl), "attention launch");
     }
     if (tc) {
-      tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, attn16, hidden, nullptr, H);
-      norm16(L.post_norm, false, false);
-      tcproj(kKindGateUp, mmc::kEpiSwiglu, L.gu, 2 * I, H, xn16, nullptr, act16, I);
-      tcproj(kKindDown, mmc::kEpiResid, L.down, H, I, act16, hidden, nullptr, H);
+      tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, attn16, hidden, nullptr, H, false);
+      tcproj(kKindGateUp, mmc::kEpiSwiglu, L.gu, 2 * I, H, h16, nullptr, act16, I, true);
+      tcproj(kKindDown, mmc::kEpiResid, L.down, H, I, act16, hidden, nullptr, H, false);
       continue;
     }
     // ---- o projection + residual
@@ -388,7 +410,6 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     gu.N = 2 * I;
     gu.K = H;
     gu.in = hidden;
-    gu.norm_w = L.post_norm;
     gu.eps = d.rms_norm_eps;
     gu.out = act;
     gu.ldo = I;
@@ -422,13 +443,14 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   sink.hist_cap = io.hist_cap;
   sink.hist_stride = io.hist_stride > 0 ? io.hist_stride : io.B;
   if (tc) {
-    norm16(c->final_norm, false, true);
     mmc::TcArgs t;
     t.W = c->lm_head;
-    t.X = xn16;
+    t.X = h16;
     t.N = int(d.vocab_size);
     t.K = H;
     t.B = io.B;
+    t.ss_in = ss;
+    t.eps = d.rms_norm_eps;
     t.logits = io.logits;
     t.argmax_part = argmax_part;
     t.counter = argmax_counter;
@@ -444,7 +466,6 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     lm.N = int(d.vocab_size);
     lm.K = H;
     lm.in = hidden;
-    lm.norm_w = c->final_norm;
     lm.eps = d.rms_norm_eps;
     lm.logits = io.logits;
     lm.argmax_part = argmax_part;
@@ -635,7 +656,7 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
   put(1, c->final_norm);
   c->lm_head = c->alloc<__half>(size_t(V * H), "lm_head");
   put(2, stage_d);
-  ck(mmc::launch_pack_rows(stage_d, c->lm_head, V, H, c->stream), "pack lm_head");
+  ck(mmc::launch_pack_rows(stage_d, c->lm_head, V, H, c->stream, c->final_norm), "pack lm_head");
   ck(cudaStreamSynchronize(c->stream), "pack");
   c->layers.assign(size_t(d.num_hidden_layers), Layer{});
   for (int l = 0; l < int(d.num_hidden_layers); ++l) {
@@ -652,13 +673,13 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
     // fused [q; k; v] rows, language_model.cpp:95-119
     L.qkv = c->alloc<__half>(size_t((Q + 2 * KV) * H), "qkv");
     put(base + 4, stage_d);
-    ck(mmc::launch_pack_rows(stage_d, L.qkv, Q, H, c->stream), "pack q");
+    ck(mmc::launch_pack_rows(stage_d, L.qkv, Q, H, c->stream, L.in_norm), "pack q");
     ck(cudaStreamSynchronize(c->stream), "pack");
     put(base + 5, stage_d);
-    ck(mmc::launch_pack_rows(stage_d, L.qkv + Q * H, KV, H, c->stream), "pack k");
+    ck(mmc::launch_pack_rows(stage_d, L.qkv + Q * H, KV, H, c->stream, L.in_norm), "pack k");
     ck(cudaStreamSynchronize(c->stream), "pack");
     put(base + 6, stage_d);
-    ck(mmc::launch_pack_rows(stage_d, L.qkv + (Q + KV) * H, KV, H, c->stream), "pack v");
+    ck(mmc::launch_pack_rows(stage_d, L.qkv + (Q + KV) * H, KV, H, c->stream, L.in_norm), "pack v");
     ck(cudaStreamSynchronize(c->stream), "pack");
     L.o = c->alloc<__half>(size_t(H * Q), "o");
     put(base + 7, stage_d);
@@ -667,7 +688,7 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
     L.gu = c->alloc<__half>(size_t(2 * I * H), "gate_up");
     put(base + 8, stage_d);
     put(base + 9, stage_d2);
-    ck(mmc::launch_pack_gate_up(stage_d, stage_d2, L.gu, I, H, c->stream), "pack gate_up");
+    ck(mmc::launch_pack_gate_up(stage_d, stage_d2, L.gu, I, H, c->stream, L.post_norm), "pack gate_up");
     ck(cudaStreamSynchronize(c->stream), "pack");
     L.down = c->alloc<__half>(size_t(H * I), "down");
     put(base + 10, stage_d);
@@ -835,7 +856,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->qkv = c->alloc<float>(size_t(max_batch) * (Q + 2 * KV), "qkv");
     c->attn = c->alloc<float>(size_t(max_batch) * Q, "attn");
     c->act = c->alloc<float>(size_t(max_batch) * I, "act");
-    c->xn16 = c->alloc<__half>(size_t(max_batch) * H, "normed activations");
+    c->h16 = c->alloc<__half>(size_t(max_batch) * H, "residual rows fp16");
     c->attn16 = c->alloc<__half>(size_t(max_batch) * Q, "attention output fp16");
     c->act16 = c->alloc<__half>(size_t(max_batch) * I, "act fp16");
     c->q16 = c->alloc<__half>(size_t(max_batch) * Q, "q fp16");
@@ -854,6 +875,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
         "attention partials");
     c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
     c->attn_work = c->alloc<unsigned>(4, "attention work queue");
+    c->ss = c->alloc<float>(size_t(max_batch) * ((H + 127) / 128), "residual sums of squares");
     ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
     ck(cudaDeviceSynchronize(), "KV init");
     c->kv_ready = true;

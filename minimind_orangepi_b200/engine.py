@@ -162,7 +162,7 @@ class DecodeEngine:
                                      logits.ctypes.data if want_logits else None))
         return nxt, logits
 
-    KERNEL_KINDS = ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "rmsnorm")
+    KERNEL_KINDS = ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "embed")
 
     def profile_step(self, seq_ids, tokens):
         """One step with per-kernel CUDA events; returns (next, {kind: (ms, launches)})."""

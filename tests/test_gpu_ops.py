@@ -42,6 +42,24 @@ def test_projection(n, k, batch):
     assert (y - ref).abs().max().item() <= tol
 
 
+@pytest.mark.parametrize("n,k,batch", [(768, 2048, 100), (768, 768, 64), (1280, 768, 128)])
+def test_projection_split_k_is_deterministic(n, k, batch):
+    """Few-tile projections split K across a thread-block cluster and sum the
+    partial accumulators in a fixed rank order: repeated runs are bit-equal."""
+    g = torch.Generator(device="cpu").manual_seed(n + k + batch)
+    w = (torch.randn(n, k, generator=g) * 0.02).half().cuda()
+    x = torch.randn(batch, k, generator=g).half().cuda()
+    outs = []
+    for _ in range(3):
+        y = torch.full((batch, n), float("nan"), device="cuda")
+        check(lib().mmc_op_projection(batch, n, k, dev(w), dev(x), dev(y), None))
+        torch.cuda.synchronize()
+        outs.append(y)
+    ref = x.float() @ w.float().t()
+    assert (outs[0] - ref).abs().max().item() <= 2e-4 * k ** 0.5
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+
+
 @pytest.mark.parametrize("batch", [1, 2, 4, 8, 64, 256])
 def test_lm_head_argmax_is_first_max_of_its_own_logits(batch):
     n, k = 6400, 768
