@@ -71,6 +71,8 @@ T* dalloc(size_t count, const char* what) {
   return static_cast<T*>(p);
 }
 
+constexpr int kMaxParts = 4;
+
 int env_int(const char* name, int dflt) {
   const char* v = std::getenv(name);
   return v && *v ? std::atoi(v) : dflt;
@@ -88,9 +90,11 @@ struct mmc_ctx {
   int device = 0;
   int num_sms = 148;
   cudaStream_t stream = nullptr;
-  cudaStream_t stream2 = nullptr;  // second part of a split batch
-  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
-  bool split_parts = true;  // run large batches as two concurrent halves
+  // parts 1.. of a split batch run on their own streams, forked from and
+  // joined back into the launch stream
+  cudaStream_t part_stream[kMaxParts - 1] = {};
+  cudaEvent_t fork_ev = nullptr, join_ev[kMaxParts - 1] = {};
+  int split_parts = 3;  // large batches run as this many concurrent parts
   std::vector<void*> allocs;
 
   // weights
@@ -222,7 +226,7 @@ struct StepIO {
   int64_t total_pages = 1, max_ctx = 1;  // attention plan inputs (whole batch)
   int attn_ctas_per_sm = 2;  // persistent attention CTAs per SM (1 when two halves share the GPU)
   int row0 = 0;  // first scratch row of this part of the batch
-  int part = 0;  // 0/1: which counter region this part uses
+  int part = 0;  // 0 .. kMaxParts-1: which counter region this part uses
 };
 
 // Batches of up to kGemvMaxBatch rows use the CUDA-core projections with
@@ -477,10 +481,10 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   if (ev) ck(cudaEventRecord(ev[evi++], s), "event record");
 }
 
-// Batches of at least 2 * kSplitMinRows rows on the tensor-core path run as two
-// independent halves on two streams (two parallel branches of the captured
-// graph): sequences never interact, so one half's latency-bound projections
-// overlap the other half's HBM-bound attention.
+// Batches of at least 2 * kSplitMinRows rows on the tensor-core path run as
+// split_parts independent parts on their own streams (parallel branches of the
+// captured graph): sequences never interact, so one part's latency-bound
+// projections overlap another part's HBM-bound attention.
 constexpr int kSplitMinRows = 32;
 
 int attn_ctas_split() {
@@ -492,48 +496,72 @@ int attn_ctas_split() {
   return v;
 }
 
-bool splits_batch(const mmc_ctx* c, int B) { return c->split_parts && B >= 2 * kSplitMinRows; }
+// number of concurrent parts a batch of B rows runs as (1: not split)
+int batch_parts(const mmc_ctx* c, int B) {
+  int p = std::min(c->split_parts, kMaxParts);
+  while (p > 1 && B < p * kSplitMinRows) --p;
+  return std::max(p, 1);
+}
+
+// rows of part i of a B-row batch cut into p parts: cuts at B * i / p rounded
+// down to 16 rows, so with B >= p * kSplitMinRows every part has >= 16 rows
+void part_rows(int B, int p, int i, int* r0, int* n) {
+  auto cut = [&](int j) { return j >= p ? B : int(int64_t(B) * j / p) / 16 * 16; };
+  *r0 = cut(i);
+  *n = cut(i + 1) - *r0;
+}
 
 void enqueue_batch(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
   const int64_t total_pages = io.total_pages, max_ctx = io.max_ctx;
-  if (!splits_batch(c, io.B)) {
+  const int P = batch_parts(c, io.B);
+  if (P == 1) {
     enqueue_step(c, io, s);
     return;
   }
-  const int h = (io.B / 2 + 15) / 16 * 16;
-  StepIO a = io, b = io;
-  a.B = h;
-  b.B = io.B - h;
-  b.row0 = io.row0 + h;
-  b.part = 1;
-  b.slots = io.slots + h;
-  b.tokens = io.tokens + h;
-  if (io.next_out) b.next_out = io.next_out + h;
-  if (io.logits) b.logits = io.logits + size_t(h) * c->d.vocab_size;
-  if (io.hist) b.hist = io.hist + h;
-  if (io.hist_step) b.hist_step = io.hist_step + 1;
-  a.hist_stride = b.hist_stride = io.B;
-  a.attn_ctas_per_sm = b.attn_ctas_per_sm = attn_ctas_split();
-  // each half plans its own attention split over about half the pages
-  a.split_tokens = plan_split(c, std::max<int64_t>(1, total_pages * h / io.B), max_ctx, &a.max_splits);
-  b.split_tokens = plan_split(c, std::max<int64_t>(1, total_pages * (io.B - h) / io.B), max_ctx, &b.max_splits);
   ck(cudaEventRecord(c->fork_ev, s), "fork");
-  ck(cudaStreamWaitEvent(c->stream2, c->fork_ev, 0), "fork");
-  enqueue_step(c, a, s);
-  enqueue_step(c, b, c->stream2);
-  ck(cudaEventRecord(c->join_ev, c->stream2), "join");
-  ck(cudaStreamWaitEvent(s, c->join_ev, 0), "join");
+  for (int i = 0; i < P; ++i) {
+    int r0, n;
+    part_rows(io.B, P, i, &r0, &n);
+    StepIO a = io;
+    a.B = n;
+    a.row0 = io.row0 + r0;
+    a.part = i;
+    a.slots = io.slots + r0;
+    a.tokens = io.tokens + r0;
+    if (io.next_out) a.next_out = io.next_out + r0;
+    if (io.logits) a.logits = io.logits + size_t(r0) * c->d.vocab_size;
+    if (io.hist) a.hist = io.hist + r0;
+    if (io.hist_step) a.hist_step = io.hist_step + i;
+    a.hist_stride = io.B;
+    a.attn_ctas_per_sm = attn_ctas_split();
+    // each part plans its own attention split over its share of the pages
+    a.split_tokens = plan_split(c, std::max<int64_t>(1, total_pages * n / io.B), max_ctx, &a.max_splits);
+    cudaStream_t ps = s;
+    if (i > 0) {
+      ps = c->part_stream[i - 1];
+      ck(cudaStreamWaitEvent(ps, c->fork_ev, 0), "fork");
+    }
+    enqueue_step(c, a, ps);
+  }
+  for (int i = 1; i < P; ++i) {
+    ck(cudaEventRecord(c->join_ev[i - 1], c->part_stream[i - 1]), "join");
+    ck(cudaStreamWaitEvent(s, c->join_ev[i - 1], 0), "join");
+  }
 }
 
 // Positions the captured / planned attention split covers for every part.
 int64_t plan_cap_tokens(const mmc_ctx* c, const StepIO& io) {
   const int64_t total_pages = io.total_pages, max_ctx = io.max_ctx;
-  if (!splits_batch(c, io.B)) return int64_t(io.max_splits) * io.split_tokens;
-  const int h = (io.B / 2 + 15) / 16 * 16;
-  int ms_a = 1, ms_b = 1;
-  const int sa = plan_split(c, std::max<int64_t>(1, total_pages * h / io.B), max_ctx, &ms_a);
-  const int sb = plan_split(c, std::max<int64_t>(1, total_pages * (io.B - h) / io.B), max_ctx, &ms_b);
-  return std::min(int64_t(ms_a) * sa, int64_t(ms_b) * sb);
+  const int P = batch_parts(c, io.B);
+  if (P == 1) return int64_t(io.max_splits) * io.split_tokens;
+  int64_t cap = INT64_MAX;
+  for (int i = 0; i < P; ++i) {
+    int r0, n, ms = 1;
+    part_rows(io.B, P, i, &r0, &n);
+    const int st = plan_split(c, std::max<int64_t>(1, total_pages * n / io.B), max_ctx, &ms);
+    cap = std::min(cap, int64_t(ms) * st);
+  }
+  return cap;
 }
 
 void require_ready(const mmc_ctx* c) {
@@ -748,10 +776,12 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     require(major == 10, MMC_ERR_CUDA, "libminimind_cuda is built for sm_100a (B200) only");
     ck(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device), "device query");
     ck(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
-    ck(cudaStreamCreateWithFlags(&c->stream2, cudaStreamNonBlocking), "stream");
+    for (int i = 0; i < kMaxParts - 1; ++i) {
+      ck(cudaStreamCreateWithFlags(&c->part_stream[i], cudaStreamNonBlocking), "stream");
+      ck(cudaEventCreateWithFlags(&c->join_ev[i], cudaEventDisableTiming), "event");
+    }
     ck(cudaEventCreateWithFlags(&c->fork_ev, cudaEventDisableTiming), "event");
-    ck(cudaEventCreateWithFlags(&c->join_ev, cudaEventDisableTiming), "event");
-    if (const char* e = std::getenv("MMC_SPLIT_BATCH")) c->split_parts = std::atoi(e) != 0;
+    c->split_parts = std::max(1, std::min(kMaxParts, env_int("MMC_SPLIT_BATCH", 3)));
     ck(mmc::gemv_init_attributes(), "gemv attributes");
     ck(mmc::gemm_tc_init_attributes(), "tensor-core projection attributes");
     ck(mmc::attention_init_attributes(), "attention attributes");
@@ -768,11 +798,14 @@ void mmc_destroy(mmc_ctx* c) {
   drop_graph(c);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_stage) cudaFreeHost(c->h_stage);
-  if (c->stream2) cudaStreamSynchronize(c->stream2);
+  for (auto ps : c->part_stream)
+    if (ps) cudaStreamSynchronize(ps);
   if (c->stream) cudaStreamDestroy(c->stream);
-  if (c->stream2) cudaStreamDestroy(c->stream2);
+  for (auto ps : c->part_stream)
+    if (ps) cudaStreamDestroy(ps);
   if (c->fork_ev) cudaEventDestroy(c->fork_ev);
-  if (c->join_ev) cudaEventDestroy(c->join_ev);
+  for (auto e : c->join_ev)
+    if (e) cudaEventDestroy(e);
   delete c;
 }
 
@@ -869,12 +902,12 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
       part_bytes = std::max(part_bytes, mmc::gemv_argmax_part_bytes(V, H, b, c->num_sms));
     part_bytes = std::max(part_bytes, mmc::tc_argmax_part_bytes(V, max_batch));
     c->argmax_part = c->alloc<uint8_t>(part_bytes, "argmax partials");
-    c->argmax_counter = c->alloc<unsigned>(2 * (size_t(max_batch) + 2), "argmax counters (two batch parts)");
+    c->argmax_counter = c->alloc<unsigned>(kMaxParts * (size_t(max_batch) + 2), "argmax counters (per batch part)");
     c->attn_part = c->alloc<float>(
         mmc::attn_part_floats(max_batch, int(d.num_key_value_heads), c->max_splits_cap, c->rep(), int(d.head_dim)),
         "attention partials");
     c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
-    c->attn_work = c->alloc<unsigned>(4, "attention work queue");
+    c->attn_work = c->alloc<unsigned>(2 * kMaxParts, "attention work queues (per batch part)");
     c->ss = c->alloc<float>(size_t(max_batch) * ((H + 127) / 128), "residual sums of squares");
     ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
     ck(cudaDeviceSynchronize(), "KV init");
@@ -1148,7 +1181,7 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     if (!c->hist) {
       c->hist_cap = 8192;
       c->hist = c->alloc<int>(size_t(c->hist_cap) * c->max_batch, "token history");
-      c->hist_step = c->alloc<int>(2, "history counters (two batch parts)");
+      c->hist_step = c->alloc<int>(kMaxParts, "history counters (per batch part)");
     }
     upload(c, c->slots, seq_ids, sizeof(int) * batch, "slots");
     c->async_slots.clear();
@@ -1202,7 +1235,7 @@ int mmc_graph_run(mmc_ctx* c, int32_t n_steps, void* stream) {
               "position exceeds max_position_embeddings");
     }
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
-    ck(cudaMemsetAsync(c->hist_step, 0, 2 * sizeof(int), st), "history reset");
+    ck(cudaMemsetAsync(c->hist_step, 0, kMaxParts * sizeof(int), st), "history reset");
     for (int i = 0; i < n_steps; ++i) ck(cudaGraphLaunch(c->graph, st), "graph launch");
     for (int s : c->graph_slots) c->h_pos[s] += n_steps;
   });
