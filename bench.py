@@ -43,6 +43,8 @@ WORKLOADS = {
                  desc="BASELINE config 4: batched decode, MiniMind2 (768 hidden, 16 layers, 8q/2kv, hd 96, "
                       "inter 2048, vocab 6400), 256 sequences, prompt lengths U[16,2048], 256 greedy steps, "
                       "paged fp16 KV"),
+    "probe": dict(shape="minimind2", n_seqs=96, prompt=(16, 512), steps=8,
+                  desc="profiling case (not a BASELINE config): MiniMind2, 96 sequences, prompt lengths U[16,512]"),
     "cfg3": dict(shape="minimind2", n_seqs=1, prompt=(128, 128), steps=1024,
                  desc="BASELINE config 3: MiniMind2 batch 1, 128-token prompt, 1024 greedy steps"),
     "cfg2": dict(shape="minimind2-small", n_seqs=1, prompt=(512, 512), steps=512,

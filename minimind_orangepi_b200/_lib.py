@@ -1,14 +1,16 @@
 """ctypes binding of libminimind_cuda.so (include/minimind_cuda.h).
 
-The library is loaded from ``minimind_orangepi_b200/lib``. If it is missing the
+The library is loaded from ``minimind_orangepi_b200/lib`` (or the path in the
+MMC_LIBRARY environment variable, e.g. a build with other tuning macros). If it is missing the
 import of anything that computes fails loudly: there is no CPU fallback.
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libminimind_cuda.so"
+LIB_PATH = Path(os.environ.get("MMC_LIBRARY") or Path(__file__).resolve().parent / "lib" / "libminimind_cuda.so")
 
 MMC_OK = 0
 STATUS = {1: "MMC_ERR_INVALID", 2: "MMC_ERR_OUT_OF_RANGE", 3: "MMC_ERR_CUDA", 4: "MMC_ERR_NO_PAGES",

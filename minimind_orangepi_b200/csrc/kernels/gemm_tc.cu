@@ -42,9 +42,11 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int UM = 128;       // UMMA M (weight rows per CTA)
 constexpr int BK = 64;        // K per stage (one 128-byte swizzle atom of fp16)
-// Stage ring depth per batch tile: at most ~96-144 KB of tiles, so a CTA of
-// this kernel can share an SM with an attention CTA (about 110 KB) when the
-// two halves of a split batch run concurrently.
+// Stage ring depth per batch tile: at most ~96-144 KB of tiles, so that a CTA
+// of this kernel can share an SM with an attention CTA (about 110 KB) when the
+// parts of a split batch run concurrently. (Measured on B200: a fifth stage
+// for small batch tiles, or an L2 prefetch of the later weight tiles, made
+// the decode step slower.)
 template <int BN>
 constexpr int stages_for() {
   return BN >= 256 ? 3 : 4;
@@ -85,6 +87,27 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// Column sums of a 32-row x 16-column block held one row per lane (x[16]):
+// a reduce-scatter butterfly (8 + 4 + 2 + 1 shuffles) leaves each lane pair
+// with one column, one more shuffle completes it. Returns the sum of column
+// colsum16_col(lane) (the same in both lanes of a pair); x is clobbered.
+__device__ __forceinline__ int colsum16_col(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+__device__ __forceinline__ float colsum16(float* x, int lane) {
+#pragma unroll
+  for (int o = 16, n = 8; o >= 2; o >>= 1, n >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float send = hi ? x[i] : x[i + n];
+      const float keep = hi ? x[i + n] : x[i];
+      x[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return x[0] + __shfl_xor_sync(0xffffffffu, x[0], 1);
+}
+
 template <int BN>
 __device__ __forceinline__ void tmem_dealloc(uint32_t tmem) {
   tc_fence_after();
@@ -279,13 +302,12 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
         }
       }
       if (want_ss) {
+        float sq[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j < nc) {
-            const float sq = warp_sum(nv[j] * nv[j]);
-            if (lane == 0) ssw_s[warp][c0 + j] = sq;
-          }
-        }
+        for (int j = 0; j < 16; ++j) sq[j] = j < nc ? nv[j] * nv[j] : 0.f;
+        const float tot = colsum16(sq, lane);
+        const int cj = colsum16_col(lane);
+        if ((lane & 1) == 0 && cj < nc) ssw_s[warp][c0 + cj] = tot;
       }
     } else if (EPI == kEpiSwiglu) {
       // gate rows 16j..16j+7 and up rows 16j+8..16j+15 sit 8 lanes apart
