@@ -200,9 +200,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
     fence_mbar_init();
   }
   __syncthreads();
-  // q heads and the appended rows come from qk_prep_kernel just before this
-  pdl_wait();
-  pdl_launch_dependents();
 
   if (warp == kConsumerWarps) {
     // ======================================================= producer warp
@@ -231,9 +228,15 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
       return (block * 32 + lane < m.nch && pidx < a.max_pages) ? a.block_table[(size_t)slot * a.max_pages + pidx]
                                                               : -1;
     };
+    // The first item and its page-table entries depend only on the work
+    // queue, positions and block tables (stable during the step), so they are
+    // fetched before waiting on qk_prep_kernel, whose q heads and appended
+    // K/V rows the page copies below read.
     StageMeta cur{}, nxt{};
     bool have_cur = fetch(cur), have_nxt = false, nxt_decoded = false;
     int cur_pages = have_cur ? load_pages(cur, 0) : -1, nxt_pages = -1;
+    pdl_wait();
+    pdl_launch_dependents();
     int chunk = 0;
     bool done = !have_cur;
     for (int c = 0;; ++c) {
@@ -301,6 +304,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
     __syncwarp();
   } else {
     // ====================================================== consumer warps
+    pdl_wait();
+    pdl_launch_dependents();
     const int g = lane >> 2, t = lane & 3;
     const float sl2 = 1.4426950408889634f / sqrtf(float(HD));
     const int r0 = warp * kTokPerWarp;
