@@ -54,6 +54,11 @@ WORKLOADS = {
 }
 
 
+# measured DRAM traffic / algorithmic bytes of attention_kernel (ncu, B=128, ctx 1024, hd 96):
+# (100.93 MB read + 5.11 MB written) / (100.66 MB K/V + 0.39 MB q and output)
+ATTN_TRAFFIC_RATIO = (100.93 + 5.11) / (100.66 + 0.39)
+
+
 def workload_prompts(w: dict, seed: int = 0):
     rng = np.random.default_rng(seed)
     lo, hi = w["prompt"]
@@ -416,7 +421,12 @@ def main() -> None:
             "roofline": {
                 "bound": "hbm", "kernel": "attention (fused q/k norm + RoPE + paged KV append + flash-decode)",
                 "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "peak_source": f"{peak_src} hbm_gbs", "traffic": None,
+                "peak_source": f"{peak_src} hbm_gbs",
+                # DRAM bytes per launch: the ratio of dram__bytes_read.sum + dram__bytes_write.sum to the
+                # algorithmic bytes in the ncu capture of profiles/attention_hd96_b128_ctx1024.md (a smaller
+                # launch of the same kernel; traffic grows with the pages read), scaled to this launch
+                "traffic": attn_bytes_per_launch * ATTN_TRAFFIC_RATIO,
+                "traffic_source": "scaled from an ncu capture of a smaller launch (ratio %.3f)" % ATTN_TRAFFIC_RATIO,
                 "bytes_per_launch": attn_bytes_per_launch, "avg_launch_ms": attn_ms,
                 "step_bytes": step_bytes, "step_frac": step_bytes / (dev_ms_max / K / 1000.0) / 1e9 / hbm,
                 "kernel_ms_per_step": {k: v[0] / args.profile_steps for k, v in prof.items()},

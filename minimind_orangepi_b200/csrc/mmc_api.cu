@@ -224,14 +224,14 @@ struct StepIO {
   int split_tokens = 64;
   int max_splits = 1;
   int64_t total_pages = 1, max_ctx = 1;  // attention plan inputs (whole batch)
-  int attn_ctas_per_sm = 2;  // persistent attention CTAs per SM (1 when two halves share the GPU)
+  int attn_ctas_per_sm = 2;  // persistent attention CTAs per SM (1 when concurrent batch parts share the GPU)
   int row0 = 0;  // first scratch row of this part of the batch
   int part = 0;  // 0 .. kMaxParts-1: which counter region this part uses
 };
 
 // Batches of up to kGemvMaxBatch rows use the CUDA-core projections with
-// fused RMSNorm prologues (6 kernels per layer); larger batches the tensor-core
-// projections behind an fp16 RMSNorm kernel (8 per layer).
+// fused RMSNorm prologues; larger batches the tensor-core projections with the
+// RMSNorms folded across kernels. Both run 6 kernels per layer.
 constexpr int kGemvMaxBatch = 4;
 enum Kind { kKindQkv = 0, kKindAttn = 1, kKindO = 2, kKindGateUp = 3, kKindDown = 4, kKindLm = 5, kKindNorm = 6 };
 
@@ -303,7 +303,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
                     int ldo, bool normed) {
     mmc::TcArgs t;
     // split-K clusters lose to plain tiles inside the decode step (measured on
-    // B200 with the two concurrent batch halves); MMC_DECODE_SPLIT_K=n allows n
+    // B200 with concurrent batch parts); MMC_DECODE_SPLIT_K=n allows n
     t.max_splits = c->decode_split_k;
     if (normed) {
       t.ss_in = ss;
