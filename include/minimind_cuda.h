@@ -145,6 +145,19 @@ MMC_EXPORT int mmc_debug_scratch(mmc_ctx* ctx, int32_t which, float* host, int64
 MMC_EXPORT int mmc_decode_step(mmc_ctx* ctx, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
                     int32_t* next_tokens, float* logits_host);
 
+/* Prompt pass on the device (replaces the token-by-token prompt loop of
+ * LanguageModel::generate_stream, language_model.cpp:368-396, and plays the
+ * role of prefill_next_token_device, language_model.cpp:229-251): feeds
+ * prompt_lens[i] tokens to each sequence seq_ids[i] (tokens concatenated in
+ * sequence order) in batched passes of up to max_batch rows, one row per
+ * prompt position. Each row attends causally to its sequence's cache up to
+ * its own position; every row's K/V is appended and the positions advance by
+ * the prompt lengths. next_tokens[i] receives the greedy token after sequence
+ * i's last prompt token (what the last mmc_decode_step of a token-by-token
+ * prompt would return). Pages are reserved as needed. Synchronous. */
+MMC_EXPORT int mmc_prefill(mmc_ctx* ctx, int32_t n_seqs, const int32_t* seq_ids, const int32_t* prompt_lens,
+                           const int32_t* tokens, int32_t* next_tokens);
+
 /* One decode step like mmc_decode_step, with a CUDA event between every two
  * kernels (programmatic overlap off) so each kernel's device time is
  * measured. kind_ms[7] / kind_launches[7] receive the summed milliseconds and

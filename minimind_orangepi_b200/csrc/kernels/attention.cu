@@ -111,7 +111,7 @@ __device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, StageMeta&
   const int bh = w % per_split;
   m.b = bh / a.nkv;
   m.h = bh % a.nkv;
-  const int ctx = a.seq_pos[a.slots[m.b]] + 1;
+  const int ctx = a.seq_pos[a.slots[m.b]] + (a.row_off ? a.row_off[m.b] : 0) + 1;
   const int pages = (ctx + kPageTokens - 1) / kPageTokens;
   const int split_pages = a.split_tokens / kPageTokens;
   m.nsplits = (pages + split_pages - 1) / split_pages;
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(128) qk_prep_kernel(AttnArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   const int slot = a.slots[b];
-  const int pos = a.seq_pos[slot];
+  const int pos = a.seq_pos[slot] + (a.row_off ? a.row_off[b] : 0);
   if (pos >= a.max_pos || pos / kPageTokens >= a.max_pages) {
     if (tid == 0) set_error(a.err, kDevPositionLimit);
     return;

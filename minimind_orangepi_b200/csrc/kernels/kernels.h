@@ -151,6 +151,7 @@ struct AttnArgs {
   int max_pages = 0;
   const int* seq_pos = nullptr;  // [max_seqs] tokens cached before this step
   const int* slots = nullptr;    // [B]
+  const int* row_off = nullptr;  // optional [B]: row b sits at seq_pos[slots[b]] + row_off[b] (prompt pass)
   int B = 0, nq = 0, nkv = 0, hd = 0;
   int split_tokens = 0;  // multiple of the page size
   int max_splits = 0;    // grid.x

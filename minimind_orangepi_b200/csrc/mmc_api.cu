@@ -123,6 +123,7 @@ struct mmc_ctx {
   __half *h16 = nullptr, *attn16 = nullptr, *act16 = nullptr;  // tensor-core path activations
   __half* q16 = nullptr;  // normalised + rotated q heads, [max_batch][nq][hd]
   int *tokens = nullptr, *slots = nullptr, *next = nullptr;
+  int* row_off = nullptr;  // [max_batch] prompt-pass position offsets
   void* argmax_part = nullptr;
   unsigned* argmax_counter = nullptr;
   float* attn_part = nullptr;
@@ -225,6 +226,7 @@ struct StepIO {
   int max_splits = 1;
   int64_t total_pages = 1, max_ctx = 1;  // attention plan inputs (whole batch)
   int attn_ctas_per_sm = 2;  // persistent attention CTAs per SM (1 when concurrent batch parts share the GPU)
+  const int* row_off = nullptr;  // prompt pass: per-row position offsets (positions advanced by the host)
   int row0 = 0;  // first scratch row of this part of the batch
   int part = 0;  // 0 .. kMaxParts-1: which counter region this part uses
 };
@@ -367,6 +369,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     a.block_table = c->d_block_table;
     a.max_pages = c->max_pages;
     a.seq_pos = c->d_seq_pos;
+    a.row_off = io.row_off;
     a.slots = io.slots;
     a.B = io.B;
     a.nq = int(d.num_attention_heads);
@@ -440,7 +443,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   mmc::TokenSink sink;
   sink.tokens = io.tokens;
   sink.next_out = io.next_out;
-  sink.seq_pos = c->d_seq_pos;
+  sink.seq_pos = io.row_off ? nullptr : c->d_seq_pos;
   sink.slots = io.slots;
   sink.hist = io.hist;
   sink.hist_step = io.hist_step;
@@ -527,6 +530,7 @@ void enqueue_batch(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
     a.row0 = io.row0 + r0;
     a.part = i;
     a.slots = io.slots + r0;
+    if (io.row_off) a.row_off = io.row_off + r0;
     a.tokens = io.tokens + r0;
     if (io.next_out) a.next_out = io.next_out + r0;
     if (io.logits) a.logits = io.logits + size_t(r0) * c->d.vocab_size;
@@ -897,6 +901,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->tokens = c->alloc<int>(size_t(max_batch), "tokens");
     c->slots = c->alloc<int>(size_t(max_batch), "slots");
     c->next = c->alloc<int>(size_t(max_batch), "next");
+    c->row_off = c->alloc<int>(size_t(max_batch), "prompt row offsets");
     size_t part_bytes = 0;
     for (int b = 1; b <= std::min(max_batch, 4); ++b)
       part_bytes = std::max(part_bytes, mmc::gemv_argmax_part_bytes(V, H, b, c->num_sms));
@@ -1083,6 +1088,96 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     check_device_error(c);
     std::memcpy(next_tokens, c->h_stage + 2 * batch, sizeof(int) * batch);
     for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
+  });
+}
+
+int mmc_prefill(mmc_ctx* c, int32_t n_seqs, const int32_t* seq_ids, const int32_t* prompt_lens, const int32_t* tokens,
+                int32_t* next_tokens) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    require_ready(c);
+    require(n_seqs >= 1 && seq_ids && prompt_lens && tokens && next_tokens, MMC_ERR_INVALID, "null argument");
+    // validate everything before anything runs
+    int64_t total = 0;
+    std::vector<char> seen(c->max_seqs, 0);
+    for (int i = 0; i < n_seqs; ++i) {
+      const int32_t s = seq_ids[i];
+      check_seq(c, s);
+      require(!seen[s], MMC_ERR_INVALID, "a sequence appears twice in one prompt pass");
+      seen[s] = 1;
+      require(prompt_lens[i] >= 1, MMC_ERR_INVALID, "empty prompt");
+      require(c->h_pos[s] + prompt_lens[i] <= c->d.max_position_embeddings, MMC_ERR_OUT_OF_RANGE,
+              "prompt exceeds max_position_embeddings");
+      total += prompt_lens[i];
+    }
+    for (int64_t t = 0; t < total; ++t)
+      require(tokens[t] >= 0 && tokens[t] < c->d.vocab_size, MMC_ERR_OUT_OF_RANGE, "token id out of vocabulary range");
+    for (int i = 0; i < n_seqs; ++i) reserve_pages(c, seq_ids[i], c->h_pos[seq_ids[i]] + prompt_lens[i]);
+
+    // rows in prompt order, packed into passes of at most max_batch rows; a
+    // row's position is its sequence's position at the start of the pass
+    // plus its offset among that sequence's rows in the pass
+    const int cap = c->max_batch;
+    int* h_slots = c->h_stage;
+    int* h_tok = c->h_stage + cap;
+    int* h_off = c->h_stage + 2 * cap;
+    int* h_next = c->h_stage + 3 * cap;
+    int si = 0, ti = 0;  // next sequence / its next prompt token
+    int64_t consumed = 0;
+    while (consumed < total) {
+      int rows = 0;
+      std::vector<std::pair<int, int>> last_rows;  // (sequence index, row) of prompts that end in this pass
+      std::vector<std::pair<int32_t, int>> advanced;  // (sequence, rows in this pass)
+      int64_t total_pages = 0, max_ctx = 1;
+      int64_t tok_base = 0;
+      for (int i = 0; i < si; ++i) tok_base += prompt_lens[i];
+      while (rows < cap && si < n_seqs) {
+        const int32_t s = seq_ids[si];
+        const int take = std::min(cap - rows, prompt_lens[si] - ti);
+        for (int k = 0; k < take; ++k) {
+          h_slots[rows + k] = s;
+          h_tok[rows + k] = tokens[tok_base + ti + k];
+          h_off[rows + k] = k;
+          const int64_t ctx = c->h_pos[s] + k + 1;
+          total_pages += (ctx + mmc::kPageTokens - 1) / mmc::kPageTokens;
+          max_ctx = std::max(max_ctx, ctx);
+        }
+        advanced.emplace_back(s, take);
+        rows += take;
+        ti += take;
+        if (ti == prompt_lens[si]) {
+          last_rows.emplace_back(si, rows - 1);
+          tok_base += prompt_lens[si];
+          ++si;
+          ti = 0;
+        }
+      }
+      ck(cudaMemcpyAsync(c->slots, h_slots, sizeof(int) * rows, cudaMemcpyHostToDevice, c->stream), "H2D slots");
+      ck(cudaMemcpyAsync(c->tokens, h_tok, sizeof(int) * rows, cudaMemcpyHostToDevice, c->stream), "H2D tokens");
+      ck(cudaMemcpyAsync(c->row_off, h_off, sizeof(int) * rows, cudaMemcpyHostToDevice, c->stream), "H2D offsets");
+      c->async_slots.clear();
+      StepIO io;
+      io.B = rows;
+      io.split_tokens = plan_split(c, total_pages, max_ctx, &io.max_splits);
+      io.total_pages = total_pages;
+      io.max_ctx = max_ctx;
+      io.slots = c->slots;
+      io.tokens = c->tokens;
+      io.row_off = c->row_off;
+      enqueue_batch(c, io, c->stream);
+      ck(cudaMemcpyAsync(h_next, c->tokens, sizeof(int) * rows, cudaMemcpyDeviceToHost, c->stream), "D2H tokens");
+      ck(cudaStreamSynchronize(c->stream), "prompt pass");
+      check_device_error(c);
+      for (const auto& [i, r] : last_rows) next_tokens[i] = h_next[r];
+      // advance the positions (host and device) by the rows each sequence had
+      for (const auto& [s, n] : advanced) {
+        c->h_pos[s] += n;
+        const int v = int(c->h_pos[s]);
+        upload(c, c->d_seq_pos + s, &v, sizeof(int), "position update");
+      }
+      consumed += rows;
+    }
   });
 }
 

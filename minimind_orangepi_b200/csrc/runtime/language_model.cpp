@@ -205,10 +205,20 @@ std::vector<int32_t> LanguageModel::forward_next_tokens(const std::vector<int32_
   return next;
 }
 
+// language_model.cpp:334-366 (prefill_next_token_device on the device build):
+// the whole prompt in batched passes on the device (mmc_prefill), then the
+// greedy token after its last position.
 int32_t LanguageModel::prefill_next_token(const std::vector<int32_t>& prompt_tokens, DecoderState& state) const {
   if (prompt_tokens.empty()) throw std::invalid_argument("prompt_tokens cannot be empty");
+  for (int32_t t : prompt_tokens)
+    if (t < 0 || t >= config_.vocab_size) throw std::out_of_range("token id out of vocabulary range");
+  bind(state);
+  const int32_t seq = state.device->id();
+  const int32_t n = static_cast<int32_t>(prompt_tokens.size());
   int32_t next = 0;
-  for (int32_t t : prompt_tokens) next = forward_next_token(t, state);
+  mmc_check(mmc_prefill(device_->ctx(), 1, &seq, &n, prompt_tokens.data(), &next));
+  state.position += n;
+  for (auto& l : state.layers) l.tokens += n;
   return next;
 }
 

@@ -218,6 +218,18 @@ class DecodeEngine:
                     first[i] = nxt[j]
         return first
 
+    def prompt_pass(self, seq_ids, prompts) -> np.ndarray:
+        """Feed whole prompts on the device in batched passes (mmc_prefill: one
+        row per prompt position, causal attention within each sequence);
+        returns the first generated token of each sequence, like prefill()."""
+        seq_ids = _i32(seq_ids)
+        lens = _i32([len(p) for p in prompts])
+        toks = _i32([int(t) for p in prompts for t in p])
+        first = np.empty(len(seq_ids), np.int32)
+        check(self.L.mmc_prefill(self.h, len(seq_ids), seq_ids.ctypes.data, lens.ctypes.data, toks.ctypes.data,
+                                 first.ctypes.data))
+        return first
+
     def generate(self, prompt, max_new_tokens: int, eos: int | None = None):
         """LanguageModel::generate on the device (greedy, eos stop)."""
         if not prompt:
@@ -227,7 +239,7 @@ class DecodeEngine:
         eos = self.config.eos_token_id if eos is None else eos
         seq = self.open_sequence(len(prompt) + max(max_new_tokens, 1))
         try:
-            nxt = int(self.prefill([seq], [list(prompt)])[0])
+            nxt = int(self.prompt_pass([seq], [list(prompt)])[0])
             out = []
             for i in range(max_new_tokens):
                 out.append(nxt)
