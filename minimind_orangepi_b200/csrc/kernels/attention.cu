@@ -124,10 +124,14 @@ __device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, StageMeta&
   return true;
 }
 
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
+
+__device__ __forceinline__ void red_add_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
@@ -187,7 +191,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
   __shared__ __align__(8) uint64_t full_bar[C::NST];
   __shared__ __align__(8) uint64_t empty_bar[C::NST];
   __shared__ StageMeta meta[C::NST];
-  __shared__ bool is_last;
+  __shared__ int merge_task, merge_ok;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int total_items = a.max_splits * a.B * a.nkv;
@@ -450,42 +454,75 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
           }
         }
       }
-      if (it.nsplits > 1) {
-        // ------------------------------------ merge splits (last arrival)
-        // The barrier orders every consumer's partial stores before thread 0's
-        // acquire-release arrival (release is cumulative); the last arrival's
-        // acquire plus the next barrier order the merge's loads after them.
-        consumer_sync();
-        if (tid == 0)
-          is_last = atom_add_acq_rel_gpu(&a.counters[(size_t)it.b * a.nkv + it.h], 1u) == unsigned(it.nsplits - 1);
-        consumer_sync();
-        if (is_last) {
-          // stage the split partials in shared memory (comb is free now) with
-          // independent coalesced loads, then merge from there
-          const int n = it.nsplits * int(pstride);
-          const bool staged = n <= int(C::comb_floats(rep));
-          if (staged) {
-            for (int i = tid; i < n; i += kConsumerWarps * 32) comb[i] = __ldcg(part_bh + i);
-            consumer_sync();
-          }
-          const float* src = staged ? comb : part_bh;
-          for (int i = tid; i < rep * HD; i += kConsumerWarps * 32) {
-            const int j = i / HD, d = i % HD;
-            float M = -1e30f;
-            for (int sp = 0; sp < it.nsplits; ++sp) M = fmaxf(M, src[sp * pstride + j * (HD + 2) + HD]);
-            float L = 0.f, O = 0.f;
-            for (int sp = 0; sp < it.nsplits; ++sp) {
-              const float* pp = src + sp * pstride + j * (HD + 2);
-              const float f = exp2f(pp[HD] - M);
-              L += pp[HD + 1] * f;
-              O += pp[d] * f;
+      consumer_sync();  // partials / outputs stored; comb is reused by the next item
+      // a split announces its partial without waiting: the merges run at the
+      // end of the kernel (below), off the page stream's critical path
+      if (it.nsplits > 1 && tid == 0) red_add_release_gpu(&a.counters[(size_t)it.b * a.nkv + it.h], 1u);
+    }
+
+    // ---------------------------------------------- tail: merge split items
+    // Once the work queue is empty every item is held by a running CTA, so
+    // waiting here for a (row, kv head)'s splits cannot deadlock. Tasks come
+    // from a second queue; each waits (bounded) for its pair's split count,
+    // merges the partials and clears the count.
+    const int pairs = a.B * a.nkv;
+    for (;;) {
+      if (tid == 0) merge_task = int(atomicAdd(&a.work[2], 1u));
+      consumer_sync();
+      const int task = merge_task;
+      consumer_sync();  // everyone has read merge_task before it is rewritten
+      if (task >= pairs) break;
+      const int b = task / a.nkv, h = task % a.nkv;
+      const int ctx = a.seq_pos[a.slots[b]] + (a.row_off ? a.row_off[b] : 0) + 1;
+      const int pages = (ctx + kPageTokens - 1) / kPageTokens;
+      const int split_pages = a.split_tokens / kPageTokens;
+      const int nsplits = (pages + split_pages - 1) / split_pages;
+      if (nsplits <= 1 || nsplits > a.max_splits) continue;
+      unsigned* cnt = &a.counters[(size_t)b * a.nkv + h];
+      if (tid == 0) {
+        merge_ok = 1;
+        if (ld_acquire_gpu(cnt) < unsigned(nsplits)) {
+          const uint64_t t0 = global_timer_ns();
+          while (ld_acquire_gpu(cnt) < unsigned(nsplits)) {
+            if (global_timer_ns() - t0 > 2000000000ull) {
+              set_error(a.err, kDevWaitTimeout);
+              merge_ok = 0;
+              break;
             }
-            put_out(j * HD + d, O / L);
+            __nanosleep(64);
           }
-          if (tid == 0) a.counters[(size_t)it.b * a.nkv + it.h] = 0u;
         }
       }
-      consumer_sync();  // comb is reused by the next item
+      consumer_sync();
+      if (merge_ok) {
+        float* part_bh = a.part + ((size_t)b * a.nkv + h) * a.max_splits * pstride;
+        const size_t out_off = (size_t)b * a.nq * HD + (size_t)h * rep * HD;
+        // stage the split partials in shared memory (independent coalesced
+        // loads), then merge from there
+        const int n = nsplits * int(pstride);
+        const bool staged = n <= int(C::comb_floats(rep));
+        if (staged) {
+          for (int i = tid; i < n; i += kConsumerWarps * 32) comb[i] = __ldcg(part_bh + i);
+          consumer_sync();
+        }
+        const float* src = staged ? comb : part_bh;
+        for (int i = tid; i < rep * HD; i += kConsumerWarps * 32) {
+          const int j = i / HD, d = i % HD;
+          float M = -1e30f;
+          for (int sp = 0; sp < nsplits; ++sp) M = fmaxf(M, src[sp * pstride + j * (HD + 2) + HD]);
+          float L = 0.f, O = 0.f;
+          for (int sp = 0; sp < nsplits; ++sp) {
+            const float* pp = src + sp * pstride + j * (HD + 2);
+            const float f = exp2f(pp[HD] - M);
+            L += pp[HD + 1] * f;
+            O += pp[d] * f;
+          }
+          if (a.out16) a.out16[out_off + j * HD + d] = __float2half_rn(O / L);
+          else a.out[out_off + j * HD + d] = O / L;
+        }
+        if (tid == 0) *cnt = 0u;
+      }
+      consumer_sync();  // comb is reused by the next task
     }
   }
 
@@ -496,6 +533,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
     if (atomicAdd(&a.work[1], 1u) == gridDim.x - 1) {
       a.work[0] = 0u;
       a.work[1] = 0u;
+      a.work[2] = 0u;
     }
   }
 }

@@ -159,7 +159,7 @@ struct AttnArgs {
   __half* out16 = nullptr;  // [B][nq * hd] fp16 when set (tensor-core path)
   float* part = nullptr;  // [B][nkv][max_splits][rep][hd + 2] split partials
   unsigned* counters = nullptr;  // [B][nkv], zero-initialised, self-resetting
-  unsigned* work = nullptr;      // [2] work-queue head and exit count, zero-initialised, self-resetting
+  unsigned* work = nullptr;      // [3] work-queue head, exit count, merge-queue head; zeroed, self-resetting
   __half* q16 = nullptr;         // [B][nq][hd] fp16 normalised + rotated q (written by the prep launch)
   int ctas_per_sm = 0;           // persistent grid size per SM (0: 2)
   int* err = nullptr;

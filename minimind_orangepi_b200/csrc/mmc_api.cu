@@ -128,7 +128,7 @@ struct mmc_ctx {
   unsigned* argmax_counter = nullptr;
   float* attn_part = nullptr;
   unsigned* attn_counters = nullptr;
-  unsigned* attn_work = nullptr;  // [2 parts][2] attention work-queue words
+  unsigned* attn_work = nullptr;  // [parts][4] attention work-queue words
   int decode_split_k = env_int("MMC_DECODE_SPLIT_K", 1);
   float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
   int* err = nullptr;
@@ -381,7 +381,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     a.out16 = tc ? attn16 : nullptr;
     a.part = attn_part;
     a.counters = attn_counters;
-    a.work = c->attn_work + 2 * io.part;
+    a.work = c->attn_work + 4 * io.part;
     a.q16 = c->q16 + r0 * Q;
     a.ctas_per_sm = io.attn_ctas_per_sm;
     a.err = c->err;
@@ -912,7 +912,7 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
         mmc::attn_part_floats(max_batch, int(d.num_key_value_heads), c->max_splits_cap, c->rep(), int(d.head_dim)),
         "attention partials");
     c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
-    c->attn_work = c->alloc<unsigned>(2 * kMaxParts, "attention work queues (per batch part)");
+    c->attn_work = c->alloc<unsigned>(4 * kMaxParts, "attention work queues (per batch part)");
     c->ss = c->alloc<float>(size_t(max_batch) * ((H + 127) / 128), "residual sums of squares");
     ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
     ck(cudaDeviceSynchronize(), "KV init");
