@@ -145,6 +145,17 @@ MMC_EXPORT int mmc_debug_scratch(mmc_ctx* ctx, int32_t which, float* host, int64
 MMC_EXPORT int mmc_decode_step(mmc_ctx* ctx, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
                     int32_t* next_tokens, float* logits_host);
 
+/* Packed-weight cache (the runtime-format fast path): mmc_save_packed writes
+ * the loaded context's device weights (fp16 rows with the RMSNorm weights
+ * folded in, interleaved gate/up, fp32 embedding and norms) to `path`;
+ * mmc_load_packed fills an unloaded context from such a file instead of
+ * reading and re-packing weights.bin (runtime_loader.cpp:110-167 reads fp32
+ * and the device path re-packs on every load, ascend_matmul.cpp:285-305). The
+ * file records the model description and the packing layout; a mismatch is
+ * MMC_ERR_INVALID / MMC_ERR_IO and leaves the context unloaded. */
+MMC_EXPORT int mmc_save_packed(mmc_ctx* ctx, const char* path);
+MMC_EXPORT int mmc_load_packed(mmc_ctx* ctx, const char* path);
+
 /* Prompt pass on the device (replaces the token-by-token prompt loop of
  * LanguageModel::generate_stream, language_model.cpp:368-396, and plays the
  * role of prefill_next_token_device, language_model.cpp:229-251): feeds

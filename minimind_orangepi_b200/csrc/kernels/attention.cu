@@ -44,6 +44,9 @@ namespace {
 // supported split: more page throughput per CTA at long contexts, but slower
 // for the batched decode step at ~1-2 K positions, where two CTAs per SM and
 // the 4-stage ring matter more).
+#ifndef MMC_ATTN_STAGES
+#define MMC_ATTN_STAGES 4  // ring stages for head_dim <= 96 (build-time tuning knob)
+#endif
 constexpr int kConsumerWarps = 4;
 constexpr int kTokPerWarp = 64 / kConsumerWarps;
 constexpr int kAttnThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
@@ -53,7 +56,7 @@ template <int HD>
 struct AttnCfg {
   static constexpr int CPR = HD / 8;                     // 16-byte chunks per row
   static constexpr int TILE = kPageTokens * HD;          // halves per K (or V) page slab
-  static constexpr int NST = HD <= 96 ? 4 : 3;           // ring stages
+  static constexpr int NST = HD <= 96 ? MMC_ATTN_STAGES : 3;  // ring stages
   static constexpr int KC = HD / 16;                     // k-chunks (S) == m-tiles (O)
   static constexpr size_t STAGE_BYTES = size_t(2) * TILE * 2;
   static constexpr size_t RING_BYTES = NST * STAGE_BYTES;

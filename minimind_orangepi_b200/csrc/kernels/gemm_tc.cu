@@ -47,9 +47,12 @@ constexpr int BK = 64;        // K per stage (one 128-byte swizzle atom of fp16)
 // parts of a split batch run concurrently. (Measured on B200: a fifth stage
 // for small batch tiles, or an L2 prefetch of the later weight tiles, made
 // the decode step slower.)
+#ifndef MMC_TC_SMALL_STAGES
+#define MMC_TC_SMALL_STAGES 4  // ring stages for batch tiles <= 32 (build-time tuning knob)
+#endif
 template <int BN>
 constexpr int stages_for() {
-  return BN >= 256 ? 3 : 4;
+  return BN >= 256 ? 3 : BN <= 32 ? MMC_TC_SMALL_STAGES : 4;
 }
 
 struct ArgBest {

@@ -29,6 +29,8 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
+#include <utility>
 #include <vector>
 
 namespace {
@@ -665,6 +667,42 @@ std::string tensor_name(const mmc_model_desc&, int i) {
   return "model.layers." + std::to_string((i - 3) / 11) + "." + tensor_suffix((i - 3) % 11);
 }
 
+void finish_load(mmc_ctx* c);
+
+// Every packed weight buffer of a loaded context, in the order of the packed
+// cache file: (device pointer slot, bytes). With allocate, the buffers are
+// allocated first (loading a cache).
+std::vector<std::pair<void**, size_t>> packed_buffers(mmc_ctx* c, bool allocate) {
+  const auto& d = c->d;
+  const size_t H = size_t(d.hidden_size), V = size_t(d.vocab_size), Q = size_t(c->q_size()),
+               KV = size_t(c->kv_size()), I = size_t(d.intermediate_size), HD = size_t(d.head_dim);
+  std::vector<std::pair<void**, size_t>> out;
+  auto add = [&](auto** slot, size_t elems) {
+    using T = std::remove_pointer_t<std::remove_reference_t<decltype(*slot)>>;
+    if (allocate) *slot = c->alloc<T>(elems, "packed weights");
+    out.emplace_back(reinterpret_cast<void**>(slot), elems * sizeof(T));
+  };
+  if (allocate) c->layers.assign(size_t(d.num_hidden_layers), Layer{});
+  add(&c->embed, V * H);
+  add(&c->final_norm, H);
+  add(&c->lm_head, V * H);
+  for (auto& L : c->layers) {
+    add(&L.in_norm, H);
+    add(&L.post_norm, H);
+    add(&L.q_norm, HD);
+    add(&L.k_norm, HD);
+    add(&L.qkv, (Q + 2 * KV) * H);
+    add(&L.o, H * Q);
+    add(&L.gu, 2 * I * H);
+    add(&L.down, H * I);
+  }
+  return out;
+}
+
+// Packed cache header: magic, packing layout version, the model description.
+constexpr char kPackedMagic[8] = {'M', 'M', 'C', 'P', 'K', '0', '0', '1'};
+constexpr uint32_t kPackedLayout = 1;  // rows fp16 RNE, norms folded, gate/up interleaved by 8
+
 // Upload all tensors; `get(i, staging)` fills host fp32 tensor i.
 template <typename Getter>
 void upload_weights(mmc_ctx* c, Getter&& get) {
@@ -727,6 +765,12 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
     ck(mmc::launch_pack_rows(stage_d, L.down, H, I, c->stream), "pack down");
     ck(cudaStreamSynchronize(c->stream), "pack");
   }
+  finish_load(c);
+}
+
+// RoPE tables and the loaded flag (after the weight buffers are filled).
+void finish_load(mmc_ctx* c) {
+  const auto& d = c->d;
   const auto cos_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, false);
   const auto sin_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, true);
   c->rope_cos = c->alloc<float>(cos_t.size(), "rope");
@@ -854,6 +898,66 @@ int mmc_load_weights_file(mmc_ctx* c, const char* path) {
       in.read(reinterpret_cast<char*>(h.data()), std::streamsize(count * 4));
       require(bool(in), MMC_ERR_IO, "failed to read " + want);
     });
+  });
+}
+
+int mmc_save_packed(mmc_ctx* c, const char* path) {
+  return guarded([&] {
+    require(c && path, MMC_ERR_INVALID, "null argument");
+    require(c->loaded, MMC_ERR_STATE, "weights are not loaded");
+    use_device(c);
+    const std::string tmp = std::string(path) + ".tmp";
+    {
+      std::ofstream out(tmp, std::ios::binary | std::ios::trunc);
+      require(bool(out), MMC_ERR_IO, "failed to create " + tmp);
+      out.write(kPackedMagic, 8);
+      out.write(reinterpret_cast<const char*>(&kPackedLayout), 4);
+      out.write(reinterpret_cast<const char*>(&c->d), sizeof(mmc_model_desc));
+      std::vector<char> host;
+      for (auto& [slot, bytes] : packed_buffers(c, false)) {
+        host.resize(bytes);
+        ck(cudaMemcpy(host.data(), *slot, bytes, cudaMemcpyDeviceToHost), "D2H packed weights");
+        const uint64_t n = bytes;
+        out.write(reinterpret_cast<const char*>(&n), 8);
+        out.write(host.data(), std::streamsize(bytes));
+      }
+      require(bool(out), MMC_ERR_IO, "failed to write " + tmp);
+    }
+    require(std::rename(tmp.c_str(), path) == 0, MMC_ERR_IO, std::string("failed to rename to ") + path);
+  });
+}
+
+int mmc_load_packed(mmc_ctx* c, const char* path) {
+  return guarded([&] {
+    require(c && path, MMC_ERR_INVALID, "null argument");
+    require(!c->loaded, MMC_ERR_STATE, "weights already loaded");
+    use_device(c);
+    std::ifstream in(path, std::ios::binary);
+    require(bool(in), MMC_ERR_IO, std::string("failed to open packed weights: ") + path);
+    char magic[8] = {};
+    uint32_t layout = 0;
+    mmc_model_desc d{};
+    in.read(magic, 8);
+    in.read(reinterpret_cast<char*>(&layout), 4);
+    in.read(reinterpret_cast<char*>(&d), sizeof(d));
+    require(bool(in) && std::memcmp(magic, kPackedMagic, 8) == 0 && layout == kPackedLayout, MMC_ERR_IO,
+            "not a packed weight cache of this library version");
+    require(std::memcmp(&d, &c->d, sizeof(d)) == 0, MMC_ERR_INVALID, "packed weights were made for another model");
+    // read everything before allocating, so a short file leaves the context unloaded
+    c->layers.assign(size_t(c->d.num_hidden_layers), Layer{});
+    auto slots = packed_buffers(c, false);  // sizes only (pointers not yet allocated)
+    std::vector<std::vector<char>> host;
+    for (auto& [slot, bytes] : slots) {
+      uint64_t n = 0;
+      in.read(reinterpret_cast<char*>(&n), 8);
+      require(bool(in) && n == bytes, MMC_ERR_IO, "packed weight cache is truncated or corrupt");
+      host.emplace_back(bytes);
+      in.read(host.back().data(), std::streamsize(bytes));
+      require(bool(in), MMC_ERR_IO, "packed weight cache is truncated");
+    }
+    auto dev = packed_buffers(c, true);
+    for (size_t i = 0; i < dev.size(); ++i) upload(c, *dev[i].first, host[i].data(), dev[i].second, "packed upload");
+    finish_load(c);
   });
 }
 

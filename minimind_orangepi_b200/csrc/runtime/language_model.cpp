@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <filesystem>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -84,7 +85,16 @@ class DeviceModel {
         }
         mmc_check(mmc_load_weights(ctx_, ptrs.data(), counts.data(), static_cast<int32_t>(ptrs.size())));
       } else {
-        mmc_check(mmc_load_weights_file(ctx_, weights_bin.c_str()));
+        // a packed cache next to weights.bin (DecodeEngine(packed_cache=True)
+        // or mmc_save_packed writes it) skips the fp32 read and re-pack when
+        // it is at least as new as weights.bin
+        namespace fs = std::filesystem;
+        const fs::path cache = fs::path(weights_bin).parent_path() / "weights.mmcpk";
+        std::error_code ec;
+        const bool fresh = fs::exists(cache, ec) &&
+                           fs::last_write_time(cache, ec) >= fs::last_write_time(fs::path(weights_bin), ec) && !ec;
+        if (!fresh || mmc_load_packed(ctx_, cache.c_str()) != MMC_OK)
+          mmc_check(mmc_load_weights_file(ctx_, weights_bin.c_str()));
       }
       const int64_t pages = std::max<int64_t>(1, (o.kv_tokens + 63) / 64) + o.max_seqs;
       mmc_check(mmc_kv_init(ctx_, pages, o.max_seqs, o.max_batch));

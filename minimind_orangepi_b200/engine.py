@@ -77,7 +77,7 @@ def _i32(a) -> np.ndarray:
 class DecodeEngine:
     def __init__(self, model_dir, device: int = 0, *, n_pages: int | None = None, max_seqs: int = 64,
                  max_batch: int = 64, eps: float | None = None, theta: float | None = None,
-                 pages_budget_tokens: int | None = None):
+                 pages_budget_tokens: int | None = None, packed_cache=None):
         self.L = lib()
         self.config = read_runtime_config(model_dir)
         if self.config.use_moe:
@@ -91,7 +91,7 @@ class DecodeEngine:
         self.h = h
         self.device = device
         try:
-            check(self.L.mmc_load_weights_file(self.h, str(Path(model_dir) / "weights.bin").encode()))
+            self.loaded_from = self._load(Path(model_dir), packed_cache)
             if n_pages is None:
                 tokens = pages_budget_tokens or max_seqs * 2048
                 n_pages = max(1, (tokens + 63) // 64 + max_seqs)
@@ -100,6 +100,25 @@ class DecodeEngine:
             self.close()
             raise
         self.max_batch = max_batch
+
+    def _load(self, model_dir: Path, packed_cache) -> str:
+        """weights.bin, or the packed cache (True: model_dir/weights.mmcpk) when
+        it is at least as new as weights.bin; a missing or stale cache is
+        rebuilt from weights.bin."""
+        bin_path = model_dir / "weights.bin"
+        if packed_cache:
+            cache = model_dir / "weights.mmcpk" if packed_cache is True else Path(packed_cache)
+            if cache.exists() and cache.stat().st_mtime >= bin_path.stat().st_mtime:
+                if self.L.mmc_load_packed(self.h, str(cache).encode()) == 0:
+                    return "packed"
+            check(self.L.mmc_load_weights_file(self.h, str(bin_path).encode()))
+            check(self.L.mmc_save_packed(self.h, str(cache).encode()))
+            return "weights.bin"
+        check(self.L.mmc_load_weights_file(self.h, str(bin_path).encode()))
+        return "weights.bin"
+
+    def save_packed(self, path) -> None:
+        check(self.L.mmc_save_packed(self.h, str(path).encode()))
 
     # ------------------------------------------------------------ lifecycle
     def close(self):
