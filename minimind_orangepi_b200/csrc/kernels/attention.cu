@@ -45,7 +45,7 @@ namespace {
 // for the batched decode step at ~1-2 K positions, where two CTAs per SM and
 // the 4-stage ring matter more).
 #ifndef MMC_ATTN_STAGES
-#define MMC_ATTN_STAGES 4  // ring stages for head_dim <= 96 (build-time tuning knob)
+#define MMC_ATTN_STAGES 3  // ring stages for head_dim <= 96 (build-time tuning knob)
 #endif
 constexpr int kConsumerWarps = 4;
 constexpr int kTokPerWarp = 64 / kConsumerWarps;

@@ -48,7 +48,7 @@ constexpr int BK = 64;        // K per stage (one 128-byte swizzle atom of fp16)
 // for small batch tiles, or an L2 prefetch of the later weight tiles, made
 // the decode step slower.)
 #ifndef MMC_TC_SMALL_STAGES
-#define MMC_TC_SMALL_STAGES 4  // ring stages for batch tiles <= 32 (build-time tuning knob)
+#define MMC_TC_SMALL_STAGES 3  // ring stages for batch tiles <= 32 (build-time tuning knob)
 #endif
 template <int BN>
 constexpr int stages_for() {

@@ -73,7 +73,7 @@ T* dalloc(size_t count, const char* what) {
   return static_cast<T*>(p);
 }
 
-constexpr int kMaxParts = 4;
+constexpr int kMaxParts = 8;
 
 int env_int(const char* name, int dflt) {
   const char* v = std::getenv(name);
@@ -96,7 +96,7 @@ struct mmc_ctx {
   // joined back into the launch stream
   cudaStream_t part_stream[kMaxParts - 1] = {};
   cudaEvent_t fork_ev = nullptr, join_ev[kMaxParts - 1] = {};
-  int split_parts = 3;  // large batches run as this many concurrent parts
+  int split_parts = 4;  // large batches run as this many concurrent parts
   std::vector<void*> allocs;
 
   // weights
@@ -829,7 +829,7 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
       ck(cudaEventCreateWithFlags(&c->join_ev[i], cudaEventDisableTiming), "event");
     }
     ck(cudaEventCreateWithFlags(&c->fork_ev, cudaEventDisableTiming), "event");
-    c->split_parts = std::max(1, std::min(kMaxParts, env_int("MMC_SPLIT_BATCH", 3)));
+    c->split_parts = std::max(1, std::min(kMaxParts, env_int("MMC_SPLIT_BATCH", 4)));
     ck(mmc::gemv_init_attributes(), "gemv attributes");
     ck(mmc::gemm_tc_init_attributes(), "tensor-core projection attributes");
     ck(mmc::attention_init_attributes(), "attention attributes");
