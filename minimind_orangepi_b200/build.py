@@ -35,6 +35,7 @@ CXX_FLAGS = ["-std=c++17", "-O3", "-fPIC", "-Wall", "-Wextra", f"-I{INCLUDE}", f
 CUDA_SOURCES = [
     CSRC / "kernels" / "gemv.cu",
     CSRC / "kernels" / "gemm_tc.cu",
+    CSRC / "kernels" / "mlp_chain.cu",
     CSRC / "kernels" / "attention.cu",
     CSRC / "kernels" / "pack.cu",
     CSRC / "mmc_api.cu",

@@ -118,6 +118,32 @@ int tc_counter_words(int N, int B);
 cudaError_t launch_gemm_tc(int epi, const TcArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t gemm_tc_init_attributes();
 
+// Back half of a decoder layer on the tensor-core path as one persistent
+// launch (o projection + residual, gate/up + SwiGLU with the folded
+// post-attention norm, down projection + residual), tasks in dependency order
+// from an atomic queue (mlp_chain.cu).
+struct ChainArgs {
+  CUtensorMap map_w[3];  // filled by launch_mlp_chain
+  CUtensorMap map_x[3];
+  const __half* Wo = nullptr;     // [H][Q]
+  const __half* Wgu = nullptr;    // [2I][H], gate/up interleaved by 8 rows, post-attention norm folded in
+  const __half* Wdown = nullptr;  // [H][I]
+  const __half* attn16 = nullptr;  // [B][Q] attention output
+  float* hidden = nullptr;  // [B][H] residual stream (updated twice)
+  __half* h16 = nullptr;    // [B][H] fp16 residual rows (written twice)
+  float* ss = nullptr;      // [B][H / 128] sums of squares (written twice)
+  __half* act16 = nullptr;  // [B][I]
+  int N[3] = {0, 0, 0}, K[3] = {0, 0, 0};  // o: H x Q, gate/up: 2I x H, down: H x I
+  int B = 0;
+  float eps = 0.f;
+  unsigned* sync = nullptr;  // chain_sync_words(B) zeroed words, self-resetting
+  int* err = nullptr;
+  int m_tiles[3] = {0, 0, 0}, n_tiles = 0;  // set by the launcher
+};
+int chain_sync_words(int B);
+cudaError_t launch_mlp_chain(const ChainArgs& a, int max_ctas, cudaStream_t stream, bool pdl);
+cudaError_t mlp_chain_init_attributes();
+
 // Layer-0 input of the tensor-core path: gathers embedding rows into the
 // residual stream, its fp16 copy and the sums of squares the first
 // projection's folded RMSNorm needs.

@@ -132,6 +132,9 @@ struct mmc_ctx {
   unsigned* attn_counters = nullptr;
   unsigned* attn_work = nullptr;  // [parts][4] attention work-queue words
   int decode_split_k = env_int("MMC_DECODE_SPLIT_K", 1);
+  unsigned* chain_sync = nullptr;  // [parts][chain_sync_words(max_batch)] projection-chain queues
+  int chain_words = 0;
+  bool mlp_chain = false;  // MMC_MLP_CHAIN at creation
   float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
   int* err = nullptr;
   int* h_stage = nullptr;  // pinned: [2][max_batch] ints
@@ -239,11 +242,26 @@ struct StepIO {
 constexpr int kGemvMaxBatch = 4;
 enum Kind { kKindQkv = 0, kKindAttn = 1, kKindO = 2, kKindGateUp = 3, kKindDown = 4, kKindLm = 5, kKindNorm = 6 };
 
+// With MMC_MLP_CHAIN=1 (read when a context is created) the tensor-core path
+// runs o / gate-up / down as one persistent launch per layer (mlp_chain.cu).
+// Measured on B200 it is faster than the three launches when timed alone, but
+// slower inside the decode-step graph at config 4 (its CTAs wait on stage
+// dependencies while holding shared memory the concurrent batch parts need),
+// so it is off by default.
+bool use_mlp_chain(const mmc_ctx* c) { return c->mlp_chain; }
+
 int kernels_per_step(const mmc_ctx* c, int B) {
   const int L = int(c->d.num_hidden_layers);
   // attention is two launches; the tensor-core path adds the layer-0
   // embedding gather (its RMSNorms are folded into the projections)
-  return B <= kGemvMaxBatch ? 6 * L + 1 : 6 * L + 2;
+  if (B <= kGemvMaxBatch) return 6 * L + 1;
+  return (use_mlp_chain(c) ? 4 : 6) * L + 2;
+}
+
+// persistent CTAs of one projection-chain launch (MMC_CHAIN_CTAS)
+int chain_ctas(const mmc_ctx* c) {
+  static const int v = env_int("MMC_CHAIN_CTAS", 0);
+  return v > 0 ? v : c->num_sms;
 }
 
 void launch_proj(mmc_ctx* c, int pro, int epi, const mmc::ProjArgs& a, cudaStream_t s, bool pdl) {
@@ -392,9 +410,30 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
       ck(mmc::launch_attention(a, s, pdl), "attention launch");
     }
     if (tc) {
-      tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, attn16, hidden, nullptr, H, false);
-      tcproj(kKindGateUp, mmc::kEpiSwiglu, L.gu, 2 * I, H, h16, nullptr, act16, I, true);
-      tcproj(kKindDown, mmc::kEpiResid, L.down, H, I, act16, hidden, nullptr, H, false);
+      if (use_mlp_chain(c)) {
+        mmc::ChainArgs ch;
+        ch.Wo = L.o;
+        ch.Wgu = L.gu;
+        ch.Wdown = L.down;
+        ch.attn16 = attn16;
+        ch.hidden = hidden;
+        ch.h16 = h16;
+        ch.ss = ss;
+        ch.act16 = act16;
+        ch.N[0] = H, ch.K[0] = Q;
+        ch.N[1] = 2 * I, ch.K[1] = H;
+        ch.N[2] = H, ch.K[2] = I;
+        ch.B = io.B;
+        ch.eps = d.rms_norm_eps;
+        ch.sync = c->chain_sync + size_t(io.part) * c->chain_words;
+        ch.err = c->err;
+        const bool pdl = mark(kKindO);
+        ck(mmc::launch_mlp_chain(ch, chain_ctas(c), s, pdl), "projection chain launch");
+      } else {
+        tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, attn16, hidden, nullptr, H, false);
+        tcproj(kKindGateUp, mmc::kEpiSwiglu, L.gu, 2 * I, H, h16, nullptr, act16, I, true);
+        tcproj(kKindDown, mmc::kEpiResid, L.down, H, I, act16, hidden, nullptr, H, false);
+      }
       continue;
     }
     // ---- o projection + residual
@@ -490,7 +529,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
 // split_parts independent parts on their own streams (parallel branches of the
 // captured graph): sequences never interact, so one part's latency-bound
 // projections overlap another part's HBM-bound attention.
-constexpr int kSplitMinRows = 32;
+constexpr int kSplitMinRows = 64;
 
 int attn_ctas_split() {
   static const int v = [] {
@@ -509,7 +548,7 @@ int batch_parts(const mmc_ctx* c, int B) {
 }
 
 // rows of part i of a B-row batch cut into p parts: cuts at B * i / p rounded
-// down to 16 rows, so with B >= p * kSplitMinRows every part has >= 16 rows
+// down to 16 rows, so with B >= p * kSplitMinRows every part has >= 48 rows
 void part_rows(int B, int p, int i, int* r0, int* n) {
   auto cut = [&](int j) { return j >= p ? B : int(int64_t(B) * j / p) / 16 * 16; };
   *r0 = cut(i);
@@ -830,8 +869,10 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     }
     ck(cudaEventCreateWithFlags(&c->fork_ev, cudaEventDisableTiming), "event");
     c->split_parts = std::max(1, std::min(kMaxParts, env_int("MMC_SPLIT_BATCH", 4)));
+    c->mlp_chain = env_int("MMC_MLP_CHAIN", 0) != 0;
     ck(mmc::gemv_init_attributes(), "gemv attributes");
     ck(mmc::gemm_tc_init_attributes(), "tensor-core projection attributes");
+    ck(mmc::mlp_chain_init_attributes(), "projection chain attributes");
     ck(mmc::attention_init_attributes(), "attention attributes");
     c->err = c->alloc<int>(1, "error word");
     ck(cudaDeviceSynchronize(), "context init");
@@ -1017,6 +1058,8 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
         "attention partials");
     c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
     c->attn_work = c->alloc<unsigned>(4 * kMaxParts, "attention work queues (per batch part)");
+    c->chain_words = mmc::chain_sync_words(max_batch);
+    c->chain_sync = c->alloc<unsigned>(size_t(kMaxParts) * c->chain_words, "projection-chain queues (per batch part)");
     c->ss = c->alloc<float>(size_t(max_batch) * ((H + 127) / 128), "residual sums of squares");
     ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
     ck(cudaDeviceSynchronize(), "KV init");
