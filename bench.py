@@ -55,8 +55,8 @@ WORKLOADS = {
 
 
 # measured DRAM traffic / algorithmic bytes of attention_kernel (ncu, B=128, ctx 1024, hd 96):
-# (100.93 MB read + 5.11 MB written) / (100.66 MB K/V + 0.39 MB q and output)
-ATTN_TRAFFIC_RATIO = (100.93 + 5.11) / (100.66 + 0.39)
+# (100.95 MB read + 7.51 MB written) / (100.66 MB K/V + 0.39 MB q and output)
+ATTN_TRAFFIC_RATIO = (100.95 + 7.51) / (100.66 + 0.39)
 
 
 def workload_prompts(w: dict, seed: int = 0):
