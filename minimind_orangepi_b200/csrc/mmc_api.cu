@@ -179,9 +179,9 @@ void require(bool ok, int code, const std::string& msg) {
   if (!ok) fail(code, msg);
 }
 
-void check_device_error(mmc_ctx* c) {
-  int e = 0;
-  ck(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+// Raises MMC_ERR_DEVICE (and clears the word) if the device error word `e`,
+// already read back, is set.
+void raise_device_error(mmc_ctx* c, int e) {
   if (e != 0) {
     ck(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream), "clear device error word");
     ck(cudaStreamSynchronize(c->stream), "clear device error word");
@@ -192,6 +192,12 @@ void check_device_error(mmc_ctx* c) {
                                                      : "unknown";
     fail(MMC_ERR_DEVICE, std::string("device error: ") + what);
   }
+}
+
+void check_device_error(mmc_ctx* c) {
+  int e = 0;
+  ck(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+  raise_device_error(c, e);
 }
 
 // Split size for the attention kernel: enough CTAs to cover the SMs a few
@@ -1227,12 +1233,15 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     }
     ck(cudaMemcpyAsync(c->h_stage + 2 * batch, c->tokens, sizeof(int) * batch, cudaMemcpyDeviceToHost, c->stream),
        "D2H next tokens");
+    // the device error word rides along with the tokens (one synchronisation per step)
+    ck(cudaMemcpyAsync(c->h_stage + 3 * batch, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream),
+       "D2H error word");
     if (logits_host)
       ck(cudaMemcpyAsync(logits_host, c->logits, sizeof(float) * batch * c->d.vocab_size, cudaMemcpyDeviceToHost,
                          c->stream),
          "D2H logits");
     ck(cudaStreamSynchronize(c->stream), "decode step");
-    check_device_error(c);
+    raise_device_error(c, c->h_stage[3 * batch]);
     std::memcpy(next_tokens, c->h_stage + 2 * batch, sizeof(int) * batch);
     for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
   });
