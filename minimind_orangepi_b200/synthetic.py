@@ -34,6 +34,8 @@ class ModelShape:
     intermediate_size: int
     vocab_size: int = 6400
     max_position_embeddings: int = 32768
+    num_experts: int = 0  # > 0: top-1 MoE MLP (use_moe=1) with this many experts
+    moe_intermediate_size: int = 0  # 0: intermediate_size
 
 
 SHAPES = {
@@ -45,7 +47,15 @@ SHAPES = {
     "tiny": ModelShape(64, 2, 4, 2, 16, 128, vocab_size=256, max_position_embeddings=4096),
     "tiny-hd64": ModelShape(256, 2, 4, 2, 64, 384, vocab_size=512, max_position_embeddings=8192),
     "tiny-hd96": ModelShape(384, 2, 4, 1, 96, 512, vocab_size=1024, max_position_embeddings=8192),
+    # top-1 MoE variants (the reference's CPU path, decoder_layer.cpp:370-389)
+    "tiny-moe": ModelShape(256, 2, 4, 2, 64, 384, vocab_size=512, max_position_embeddings=8192, num_experts=4,
+                           moe_intermediate_size=256),
+    "minimind2-small-moe": ModelShape(512, 8, 8, 2, 64, 1408, num_experts=4, moe_intermediate_size=1408),
 }
+
+
+def moe_inter(s: ModelShape) -> int:
+    return s.moe_intermediate_size or s.intermediate_size
 
 
 def tensor_order(s: ModelShape) -> list[tuple[str, tuple[int, ...]]]:
@@ -62,10 +72,20 @@ def tensor_order(s: ModelShape) -> list[tuple[str, tuple[int, ...]]]:
             (p + "self_attn.k_proj.weight", (kv, h)),
             (p + "self_attn.v_proj.weight", (kv, h)),
             (p + "self_attn.o_proj.weight", (h, q)),
-            (p + "mlp.gate_proj.weight", (i, h)),
-            (p + "mlp.up_proj.weight", (i, h)),
-            (p + "mlp.down_proj.weight", (h, i)),
         ]
+        if s.num_experts > 0:  # export_minimind_runtime.py:128-138
+            mi = moe_inter(s)
+            out.append((p + "mlp.gate.weight", (s.num_experts, h)))
+            for e in range(s.num_experts):
+                ep = p + f"mlp.experts.{e}."
+                out += [(ep + "gate_proj.weight", (mi, h)), (ep + "up_proj.weight", (mi, h)),
+                        (ep + "down_proj.weight", (h, mi))]
+        else:
+            out += [
+                (p + "mlp.gate_proj.weight", (i, h)),
+                (p + "mlp.up_proj.weight", (i, h)),
+                (p + "mlp.down_proj.weight", (h, i)),
+            ]
     return out
 
 
@@ -87,7 +107,7 @@ def write_runtime_config(s: ModelShape, out: Path, eps: float | None, theta: flo
     lines = [
         f"hidden_size={s.hidden_size}",
         f"num_hidden_layers={s.num_hidden_layers}",
-        "use_moe=0",
+        f"use_moe={1 if s.num_experts > 0 else 0}",
         f"vocab_size={s.vocab_size}",
         f"num_attention_heads={s.num_attention_heads}",
         f"num_key_value_heads={s.num_key_value_heads}",
@@ -95,9 +115,9 @@ def write_runtime_config(s: ModelShape, out: Path, eps: float | None, theta: flo
         f"intermediate_size={s.intermediate_size}",
         f"max_position_embeddings={s.max_position_embeddings}",
         "tie_word_embeddings=1",
-        "num_experts=4",
+        f"num_experts={s.num_experts if s.num_experts > 0 else 4}",
         "num_experts_per_tok=1",
-        f"moe_intermediate_size={s.intermediate_size}",
+        f"moe_intermediate_size={moe_inter(s)}",
     ]
     if eps is not None:
         lines.append(f"rms_norm_eps={eps!r}")

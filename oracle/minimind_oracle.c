@@ -24,6 +24,7 @@
 typedef struct {
   int64_t hidden, layers, vocab, nq, nkv, hd, inter, max_pos;
   float eps, theta;
+  int64_t use_moe, experts, moe_inter; /* top-1 MoE MLP (runtime_loader.cpp:76,84-86) */
 } mmo_config;
 
 typedef struct {
@@ -32,6 +33,8 @@ typedef struct {
   float *o;       /* [hidden][nq*hd] */
   float *gate_up; /* fused [gate;up] rows */
   float *down;    /* [hidden][inter] */
+  float *moe_gate;            /* [experts][hidden] router */
+  float **exp_gate_up, **exp_down; /* per expert: fused [gate;up] rows, down */
 } mmo_layer;
 
 typedef struct {
@@ -235,11 +238,9 @@ MMO_API mmo_model *mmo_load(const char *dir, float eps, float theta) {
   c->max_pos = kv_get(text, "max_position_embeddings", 32768);
   c->eps = eps > 0.0f ? eps : 1e-6f;
   c->theta = theta > 0.0f ? theta : 1000000.0f;
-  if (kv_get(text, "use_moe", 0)) {
-    snprintf(g_err, sizeof g_err, "MoE checkpoints are out of scope");
-    free(m);
-    return NULL;
-  }
+  c->use_moe = kv_get(text, "use_moe", 0);
+  c->experts = kv_get(text, "num_experts", 4);
+  c->moe_inter = kv_get(text, "moe_intermediate_size", c->inter);
   snprintf(path, sizeof path, "%s/weights.bin", dir);
   f = fopen(path, "rb");
   if (!f) {
@@ -276,14 +277,32 @@ MMO_API mmo_model *mmo_load(const char *dir, float eps, float theta) {
     RD(kp, "self_attn.k_proj.weight", KV * H);
     RD(vp, "self_attn.v_proj.weight", KV * H);
     RD(L->o, "self_attn.o_proj.weight", H * Q);
-    RD(gp, "mlp.gate_proj.weight", I * H);
-    RD(up, "mlp.up_proj.weight", I * H);
-    RD(L->down, "mlp.down_proj.weight", H * I);
+    if (c->use_moe) { /* runtime_loader.cpp:148-158; experts fused as language_model.cpp:110-116 */
+      const int64_t MI = c->moe_inter;
+      RD(L->moe_gate, "mlp.gate.weight", c->experts * H);
+      L->exp_gate_up = (float **)calloc((size_t)c->experts, sizeof(float *));
+      L->exp_down = (float **)calloc((size_t)c->experts, sizeof(float *));
+      for (int64_t e = 0; ok && e < c->experts; ++e) {
+        char ep[64];
+        float *eg = NULL, *eu = NULL;
+        snprintf(ep, sizeof ep, "mlp.experts.%lld.gate_proj.weight", (long long)e);
+        RD(eg, ep, MI * H);
+        snprintf(ep, sizeof ep, "mlp.experts.%lld.up_proj.weight", (long long)e);
+        RD(eu, ep, MI * H);
+        snprintf(ep, sizeof ep, "mlp.experts.%lld.down_proj.weight", (long long)e);
+        RD(L->exp_down[e], ep, H * MI);
+        if (ok) L->exp_gate_up[e] = concat2(eg, (size_t)(MI * H), eu, (size_t)(MI * H));
+      }
+    } else {
+      RD(gp, "mlp.gate_proj.weight", I * H);
+      RD(up, "mlp.up_proj.weight", I * H);
+      RD(L->down, "mlp.down_proj.weight", H * I);
+    }
 #undef RD
     if (ok) {
       L->qkv = concat2(concat2(qp, (size_t)(Q * H), kp, (size_t)(KV * H)), (size_t)((Q + KV) * H), vp,
                        (size_t)(KV * H));
-      L->gate_up = concat2(gp, (size_t)(I * H), up, (size_t)(I * H));
+      if (!c->use_moe) L->gate_up = concat2(gp, (size_t)(I * H), up, (size_t)(I * H));
     }
   }
   fclose(f);
@@ -300,7 +319,12 @@ MMO_API void mmo_free(mmo_model *m) {
   for (int64_t l = 0; l < m->c.layers; ++l) {
     mmo_layer *L = &m->layer[l];
     free(L->input_norm); free(L->post_norm); free(L->q_norm); free(L->k_norm);
-    free(L->qkv); free(L->o); free(L->gate_up); free(L->down);
+    free(L->qkv); free(L->o); free(L->gate_up); free(L->down); free(L->moe_gate);
+    for (int64_t e = 0; L->exp_gate_up && e < m->c.experts; ++e) {
+      free(L->exp_gate_up[e]);
+      free(L->exp_down[e]);
+    }
+    free(L->exp_gate_up); free(L->exp_down);
   }
   free(m->layer); free(m->embed); free(m->final_norm); free(m->lm_head);
   free(m->rope_cos); free(m->rope_sin);
@@ -341,7 +365,8 @@ static void cache_append(mmo_cache *c, const float *k, const float *v, int64_t r
 /* decoder_layer.cpp:312-407 run_dense_decoder_layer (dense, fused weights). */
 static void decoder_layer(const mmo_model *m, const mmo_layer *L, mmo_cache *cache, float *hidden, int64_t pos) {
   const mmo_config *c = &m->c;
-  const int64_t H = c->hidden, Q = c->nq * c->hd, KV = c->nkv * c->hd, I = c->inter;
+  const int64_t H = c->hidden, Q = c->nq * c->hd, KV = c->nkv * c->hd;
+  const int64_t I = c->use_moe ? (c->moe_inter > c->inter ? c->moe_inter : c->inter) : c->inter;
   float *normed = (float *)malloc((size_t)H * sizeof(float));
   float *qkv = (float *)malloc((size_t)(Q + 2 * KV) * sizeof(float));
   float *ctx = (float *)malloc((size_t)Q * sizeof(float));
@@ -364,9 +389,20 @@ static void decoder_layer(const mmo_model *m, const mmo_layer *L, mmo_cache *cac
   for (int64_t i = 0; i < H; ++i) hidden[i] = hidden[i] + attn[i];           /* :364-367 */
   memcpy(normed, hidden, (size_t)H * sizeof(float));
   mmo_rms_norm_inplace(normed, L->post_norm, H, c->eps);                      /* :369 */
-  mmo_matvec(L->gate_up, 2 * I, H, normed, gu);                               /* :392-393 */
-  mmo_swiglu(gu, I, act);                                                     /* :394 */
-  mmo_matvec(L->down, H, I, act, mlp);                                        /* :400 */
+  if (c->use_moe) { /* :370-389: router argmax (first max), the chosen expert's MLP, no gate weighting */
+    float *router = (float *)malloc((size_t)c->experts * sizeof(float));
+    mmo_matvec(L->moe_gate, c->experts, H, normed, router);
+    const int64_t e = mmo_argmax(router, c->experts);
+    free(router);
+    const int64_t MI = c->moe_inter;
+    mmo_matvec(L->exp_gate_up[e], 2 * MI, H, normed, gu);
+    mmo_swiglu(gu, MI, act);
+    mmo_matvec(L->exp_down[e], H, MI, act, mlp);
+  } else {
+    mmo_matvec(L->gate_up, 2 * I, H, normed, gu);                             /* :392-393 */
+    mmo_swiglu(gu, I, act);                                                   /* :394 */
+    mmo_matvec(L->down, H, I, act, mlp);                                      /* :400 */
+  }
   for (int64_t i = 0; i < H; ++i) hidden[i] += mlp[i];                        /* :403-405 */
   free(normed); free(qkv); free(ctx); free(attn); free(gu); free(act); free(mlp);
 }

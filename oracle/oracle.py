@@ -25,7 +25,7 @@ REF_CLI = HERE / "_ref" / "minimind_generate_ref"
 
 class MmoConfig(C.Structure):
     _fields_ = [(n, C.c_int64) for n in ("hidden", "layers", "vocab", "nq", "nkv", "hd", "inter", "max_pos")] + [
-        ("eps", C.c_float), ("theta", C.c_float)]
+        ("eps", C.c_float), ("theta", C.c_float)] + [(n, C.c_int64) for n in ("use_moe", "experts", "moe_inter")]
 
 
 _lib = None

@@ -106,7 +106,6 @@ void* mmref_load(const char* model_dir, float eps, float theta) {
     c.moe_intermediate_size = geti(kv, "moe_intermediate_size", c.intermediate_size);
     if (eps > 0.0F) c.rms_norm_eps = eps;
     if (theta > 0.0F) c.rope_theta = theta;
-    if (c.use_moe) throw std::invalid_argument("oracle driver: MoE checkpoints are out of scope");
 
     std::ifstream in(dir + "/weights.bin", std::ios::binary);
     if (!in) throw std::runtime_error("failed to open runtime weights");
@@ -128,9 +127,21 @@ void* mmref_load(const char* model_dir, float eps, float theta) {
       lw.k_proj = read_tensor(in, p + "self_attn.k_proj.weight");
       lw.v_proj = read_tensor(in, p + "self_attn.v_proj.weight");
       lw.o_proj = read_tensor(in, p + "self_attn.o_proj.weight");
-      lw.gate_proj = read_tensor(in, p + "mlp.gate_proj.weight");
-      lw.up_proj = read_tensor(in, p + "mlp.up_proj.weight");
-      lw.down_proj = read_tensor(in, p + "mlp.down_proj.weight");
+      if (c.use_moe) {  // tensor order of runtime_loader.cpp:148-158
+        lw.moe_gate = read_tensor(in, p + "mlp.gate.weight");
+        for (int64_t e = 0; e < c.num_experts; ++e) {
+          const std::string ep = p + "mlp.experts." + std::to_string(e) + ".";
+          mm::ExpertWeights ew;
+          ew.gate_proj = read_tensor(in, ep + "gate_proj.weight");
+          ew.up_proj = read_tensor(in, ep + "up_proj.weight");
+          ew.down_proj = read_tensor(in, ep + "down_proj.weight");
+          lw.experts.push_back(std::move(ew));
+        }
+      } else {
+        lw.gate_proj = read_tensor(in, p + "mlp.gate_proj.weight");
+        lw.up_proj = read_tensor(in, p + "mlp.up_proj.weight");
+        lw.down_proj = read_tensor(in, p + "mlp.down_proj.weight");
+      }
       w.layers.push_back(std::move(lw));
     }
     return new RefModel{mm::LanguageModel(c, std::move(w))};

@@ -5,7 +5,7 @@ by oracle/build_ref.sh into oracle/_ref/) on seeded synthetic models and
 records what it produced. Needs the reference sources on this machine; the
 committed .npz files are what the tests use everywhere else.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [case ...]
 """
 from __future__ import annotations
 
@@ -31,6 +31,7 @@ CASES = {
     "tiny-hd64": ("tiny-hd64", 3, 8, 40, 12, None),
     "tiny-hd96-page-cross": ("tiny-hd96", 2, 9, 70, 10, [0, 63, 64, 65, 79]),
     "cfg1-minimind2-small": ("minimind2-small", 1, 5, 5, 16, [4, 19]),
+    "tiny-moe": ("tiny-moe", 4, 11, 30, 12, None),
 }
 EPS, THETA = 1e-5, 1e6
 
@@ -83,6 +84,8 @@ def toy_cli():
 
 
 if __name__ == "__main__":
-    for name, case in CASES.items():
-        run_case(name, *case)
-    toy_cli()
+    # python tests/golden/make_golden.py [case ...]   (default: every case and the toy CLI answer)
+    for name in sys.argv[1:] or list(CASES):
+        run_case(name, *CASES[name])
+    if len(sys.argv) == 1:
+        toy_cli()

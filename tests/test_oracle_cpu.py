@@ -21,7 +21,7 @@ from oracle.oracle import Oracle, ReferenceModel, ref_available, REF_CLI
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden"
 REFERENCE = Path(os.environ.get("MINIMIND_REFERENCE_ROOT", "/root/reference"))
-GOLDEN_CASES = ["tiny", "tiny-hd64", "tiny-hd96-page-cross", "cfg1-minimind2-small"]
+GOLDEN_CASES = ["tiny", "tiny-hd64", "tiny-hd96-page-cross", "cfg1-minimind2-small", "tiny-moe"]
 
 
 def golden_model(name, tmp_root):
