@@ -145,6 +145,14 @@ MMC_EXPORT int mmc_debug_scratch(mmc_ctx* ctx, int32_t which, float* host, int64
 MMC_EXPORT int mmc_decode_step(mmc_ctx* ctx, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
                     int32_t* next_tokens, float* logits_host);
 
+/* Top-1 mixture-of-experts MLP (the reference's use_moe path,
+ * decoder_layer.cpp:370-389, tensors in runtime_loader.cpp:148-158 order):
+ * call after mmc_create and before loading weights. Each layer's MLP becomes
+ * a router projection (num_experts rows; the first maximum picks the expert,
+ * no gate weighting) followed by the chosen expert's gate/up + SwiGLU + down.
+ * moe_intermediate_size must be a multiple of 64. */
+MMC_EXPORT int mmc_configure_moe(mmc_ctx* ctx, int32_t num_experts, int64_t moe_intermediate_size);
+
 /* Packed-weight cache (the runtime-format fast path): mmc_save_packed writes
  * the loaded context's device weights (fp16 rows with the RMSNorm weights
  * folded in, interleaved gate/up, fp32 embedding and norms) to `path`;

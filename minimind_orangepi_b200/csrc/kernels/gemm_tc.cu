@@ -193,16 +193,23 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
         if (j < nc && row < a.N && b < a.B) a.out[size_t(b) * a.ldo + row] = v[j];
       }
     } else if (EPI == kEpiResid) {
+      // row_sel (MoE): only rows routed to expert row_sel_val are updated
+      bool upd[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int b = n0 + c0 + j;
+        upd[j] = j < nc && row < a.N && b < a.B && (a.row_sel == nullptr || a.row_sel[b] == a.row_sel_val);
+      }
       float nv[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int b = n0 + c0 + j;
-        nv[j] = (j < nc && row < a.N && b < a.B) ? a.out[size_t(b) * a.ldo + row] : 0.f;
+        nv[j] = upd[j] ? a.out[size_t(b) * a.ldo + row] : 0.f;
       }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int b = n0 + c0 + j;
-        if (j < nc && row < a.N && b < a.B) {
+        if (upd[j]) {
           nv[j] += v[j];
           a.out[size_t(b) * a.ldo + row] = nv[j];
           if (a.h16_out) a.h16_out[size_t(b) * a.N + row] = __float2half_rn(nv[j]);
@@ -307,7 +314,7 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
   if (want_ss) {
     __syncthreads();
     for (int c = c_lo + tid; c < c_hi; c += kThreads)
-      if (n0 + c < a.B)
+      if (n0 + c < a.B && (a.row_sel == nullptr || a.row_sel[n0 + c] == a.row_sel_val))
         a.ss_out[size_t(n0 + c) * gridDim.x + blockIdx.x] = ssw_s[0][c] + ssw_s[1][c] + ssw_s[2][c] + ssw_s[3][c];
   }
   if (EPI != kEpiArgmax) return;

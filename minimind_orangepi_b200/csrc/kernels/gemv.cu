@@ -207,8 +207,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(ProjArgs a, int rows_per
         a.out[size_t(b) * a.ldo + g0] = acc0[b];
         if (has1) a.out[size_t(b) * a.ldo + g1] = acc1[b];
       } else if (EPI == kEpiResid) {
-        a.out[size_t(b) * a.ldo + g0] += acc0[b];
-        if (has1) a.out[size_t(b) * a.ldo + g1] += acc1[b];
+        if (a.row_sel == nullptr || a.row_sel[b] == a.row_sel_val) {  // MoE: rows routed to this expert
+          a.out[size_t(b) * a.ldo + g0] += acc0[b];
+          if (has1) a.out[size_t(b) * a.ldo + g1] += acc1[b];
+        }
       } else if (EPI == kEpiSwiglu) {
         const float g = acc0[b];
         const int i = (g0 >> 4) * 8 + (g0 & 7);

@@ -62,6 +62,8 @@ struct ProjArgs {
   // epilogue
   float* out = nullptr;  // [B][ldo]
   int ldo = 0;
+  const int* row_sel = nullptr;  // kEpiResid: update only rows b with row_sel[b] == row_sel_val (MoE)
+  int row_sel_val = 0;
   float* logits = nullptr;  // kEpiArgmax: optional [B][N]
   void* argmax_part = nullptr;  // kEpiArgmax scratch: [B][grid] (value, index)
   unsigned* counter = nullptr;  // kEpiArgmax: zero-initialised arrival counter
@@ -108,6 +110,8 @@ struct TcArgs {
   float eps = 0.f;
   __half* h16_out = nullptr;
   float* ss_out = nullptr;
+  const int* row_sel = nullptr;  // kEpiResid: update only rows b with row_sel[b] == row_sel_val (MoE)
+  int row_sel_val = 0;
 };
 int tc_batch_tile(int N, int B);
 // split-K factor the launcher uses for this projection (1 = none)

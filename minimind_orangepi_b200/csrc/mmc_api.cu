@@ -83,6 +83,8 @@ int env_int(const char* name, int dflt) {
 struct Layer {
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   __half *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+  __half* router = nullptr;                 // MoE: [experts][H] (post-attention norm folded in)
+  std::vector<__half*> egu, edown;          // MoE: per expert [2 MI][H] (interleaved, folded), [H][MI]
 };
 
 }  // namespace
@@ -97,6 +99,9 @@ struct mmc_ctx {
   cudaStream_t part_stream[kMaxParts - 1] = {};
   cudaEvent_t fork_ev = nullptr, join_ev[kMaxParts - 1] = {};
   int split_parts = 4;  // large batches run as this many concurrent parts
+  int moe_experts = 0;    // > 0: top-1 MoE MLP (mmc_configure_moe)
+  int64_t moe_inter = 0;
+  int* expert_ids = nullptr;  // [max_batch] routed expert per row
   std::vector<void*> allocs;
 
   // weights
@@ -260,6 +265,10 @@ int kernels_per_step(const mmc_ctx* c, int B) {
   const int L = int(c->d.num_hidden_layers);
   // attention is two launches; the tensor-core path adds the layer-0
   // embedding gather (its RMSNorms are folded into the projections)
+  if (c->moe_experts > 0) {  // o, router and gate/up + down per expert replace the dense MLP
+    const int per = 5 + 2 * c->moe_experts;
+    return B <= kGemvMaxBatch ? per * L + 1 : per * L + 2;
+  }
   if (B <= kGemvMaxBatch) return 6 * L + 1;
   return (use_mlp_chain(c) ? 4 : 6) * L + 2;
 }
@@ -287,15 +296,17 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   float* const hidden = c->hidden + r0 * H;
   float* const qkv = c->qkv + r0 * NQKV;
   float* const attn = c->attn + r0 * Q;
-  float* const act = c->act + r0 * I;
+  const size_t IA = size_t(std::max<int64_t>(I, c->moe_inter));  // activation row capacity (dense or expert)
+  float* const act = c->act + r0 * IA;
   __half* const h16 = c->h16 + r0 * H;
   __half* const attn16 = c->attn16 + r0 * Q;
-  __half* const act16 = c->act16 + r0 * I;
+  __half* const act16 = c->act16 + r0 * IA;
   float* const attn_part = c->attn_part + r0 * size_t(d.num_key_value_heads) * c->max_splits_cap * c->rep() *
                                                 size_t(d.head_dim + 2);
   unsigned* const attn_counters = c->attn_counters + r0 * size_t(d.num_key_value_heads);
   void* const argmax_part = static_cast<uint8_t*>(c->argmax_part) + r0 * size_t((d.vocab_size + 127) / 128) * 8;
   unsigned* const argmax_counter = c->argmax_counter + size_t(io.part) * size_t(c->max_batch + 2);
+  int* const expert_ids = c->expert_ids + r0;  // MoE: routed expert per row
   const bool tc = io.B > kGemvMaxBatch;
   int evi = 0;
   bool first = true;
@@ -328,8 +339,10 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   // normed: the input is the residual stream (scale by 1/rms); resid: update
   // the residual stream and emit its fp16 copy and sums of squares
   auto tcproj = [&](Kind k, int epi, const __half* W, int N, int K, const __half* X, float* out, __half* out16,
-                    int ldo, bool normed) {
+                    int ldo, bool normed, const int* row_sel = nullptr, int row_sel_val = 0) {
     mmc::TcArgs t;
+    t.row_sel = row_sel;
+    t.row_sel_val = row_sel_val;
     // split-K clusters lose to plain tiles inside the decode step (measured on
     // B200 with concurrent batch parts); MMC_DECODE_SPLIT_K=n allows n
     t.max_splits = c->decode_split_k;
@@ -416,7 +429,33 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
       ck(mmc::launch_attention(a, s, pdl), "attention launch");
     }
     if (tc) {
-      if (use_mlp_chain(c)) {
+      if (c->moe_experts > 0) {
+        tcproj(kKindO, mmc::kEpiResid, L.o, H, Q, attn16, hidden, nullptr, H, false);
+        // top-1 MoE (decoder_layer.cpp:370-389): router argmax -> expert id per
+        // row, then every expert's gate/up + down over the batch with the
+        // residual update committed only for the rows routed to it
+        mmc::TcArgs r;
+        r.W = L.router;
+        r.X = h16;
+        r.N = c->moe_experts;
+        r.K = H;
+        r.B = io.B;
+        r.ss_in = ss;
+        r.eps = d.rms_norm_eps;
+        r.argmax_part = argmax_part;
+        r.counter = argmax_counter;
+        r.sink.tokens = expert_ids;
+        r.err = c->err;
+        {
+          const bool pdl = mark(kKindGateUp);
+          ck(mmc::launch_gemm_tc(mmc::kEpiArgmax, r, s, pdl), "router launch");
+        }
+        const int MI = int(c->moe_inter);
+        for (int e = 0; e < c->moe_experts; ++e) {
+          tcproj(kKindGateUp, mmc::kEpiSwiglu, L.egu[e], 2 * MI, H, h16, nullptr, act16, MI, true);
+          tcproj(kKindDown, mmc::kEpiResid, L.edown[e], H, MI, act16, hidden, nullptr, H, false, expert_ids, e);
+        }
+      } else if (use_mlp_chain(c)) {
         mmc::ChainArgs ch;
         ch.Wo = L.o;
         ch.Wgu = L.gu;
@@ -455,6 +494,57 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     {
       const bool pdl = mark(kKindO);
       launch_proj(c, mmc::kProPlain, mmc::kEpiResid, o, s, pdl);
+    }
+    if (c->moe_experts > 0) {
+      // top-1 MoE: router argmax per row, then each expert masked to its rows
+      mmc::ProjArgs r;
+      r.B = io.B;
+      r.err = c->err;
+      r.W = L.router;
+      r.N = c->moe_experts;
+      r.K = H;
+      r.in = hidden;
+      r.eps = d.rms_norm_eps;
+      r.argmax_part = argmax_part;
+      r.counter = argmax_counter;
+      r.sink.tokens = expert_ids;
+      {
+        const bool pdl = mark(kKindGateUp);
+        launch_proj(c, mmc::kProNormFinal, mmc::kEpiArgmax, r, s, pdl);
+      }
+      const int MI = int(c->moe_inter);
+      for (int e = 0; e < c->moe_experts; ++e) {
+        mmc::ProjArgs eg;
+        eg.B = io.B;
+        eg.err = c->err;
+        eg.W = L.egu[e];
+        eg.N = 2 * MI;
+        eg.K = H;
+        eg.in = hidden;
+        eg.eps = d.rms_norm_eps;
+        eg.out = act;
+        eg.ldo = MI;
+        {
+          const bool pdl = mark(kKindGateUp);
+          launch_proj(c, mmc::kProNorm, mmc::kEpiSwiglu, eg, s, pdl);
+        }
+        mmc::ProjArgs ed;
+        ed.B = io.B;
+        ed.err = c->err;
+        ed.W = L.edown[e];
+        ed.N = H;
+        ed.K = MI;
+        ed.in = act;
+        ed.out = hidden;
+        ed.ldo = H;
+        ed.row_sel = expert_ids;
+        ed.row_sel_val = e;
+        {
+          const bool pdl = mark(kKindDown);
+          launch_proj(c, mmc::kProPlain, mmc::kEpiResid, ed, s, pdl);
+        }
+      }
+      continue;
     }
     // ---- gate/up + SiLU*mul
     mmc::ProjArgs gu;
@@ -694,22 +784,36 @@ const char* tensor_suffix(int i) {
   return names[i];
 }
 
+// tensors per layer in weights.bin: 8 attention/norm tensors, then the MLP --
+// dense gate/up/down, or (MoE, runtime_loader.cpp:148-158) the router and
+// each expert's gate/up/down
+int layer_tensors(const mmc_ctx* c) { return c->moe_experts > 0 ? 9 + 3 * c->moe_experts : 11; }
+int tensor_total(const mmc_ctx* c) { return 3 + layer_tensors(c) * int(c->d.num_hidden_layers); }
+
 // expected element count of tensor i in weights.bin order
-int64_t expected_count(const mmc_model_desc& d, int i) {
+int64_t expected_count(const mmc_ctx* c, int i) {
+  const auto& d = c->d;
   const int64_t H = d.hidden_size, V = d.vocab_size, Q = d.num_attention_heads * d.head_dim,
                 KV = d.num_key_value_heads * d.head_dim, I = d.intermediate_size, HD = d.head_dim;
   if (i == 0 || i == 2) return V * H;
   if (i == 1) return H;
-  const int j = (i - 3) % 11;
+  const int j = (i - 3) % layer_tensors(c);
   const int64_t counts[11] = {H, H, HD, HD, Q * H, KV * H, KV * H, H * Q, I * H, I * H, H * I};
-  return counts[j];
+  if (j < 8 || c->moe_experts == 0) return counts[j];
+  if (j == 8) return int64_t(c->moe_experts) * H;
+  return (j - 9) % 3 == 2 ? H * c->moe_inter : c->moe_inter * H;
 }
 
-std::string tensor_name(const mmc_model_desc&, int i) {
+std::string tensor_name(const mmc_ctx* c, int i) {
   if (i == 0) return "model.embed_tokens.weight";
   if (i == 1) return "model.norm.weight";
   if (i == 2) return "lm_head.weight";
-  return "model.layers." + std::to_string((i - 3) / 11) + "." + tensor_suffix((i - 3) % 11);
+  const int lt = layer_tensors(c), j = (i - 3) % lt;
+  const std::string p = "model.layers." + std::to_string((i - 3) / lt) + ".";
+  if (j < 8 || c->moe_experts == 0) return p + tensor_suffix(j);
+  if (j == 8) return p + "mlp.gate.weight";
+  static const char* part[3] = {"gate_proj.weight", "up_proj.weight", "down_proj.weight"};
+  return p + "mlp.experts." + std::to_string((j - 9) / 3) + "." + part[(j - 9) % 3];
 }
 
 void finish_load(mmc_ctx* c);
@@ -738,24 +842,37 @@ std::vector<std::pair<void**, size_t>> packed_buffers(mmc_ctx* c, bool allocate)
     add(&L.k_norm, HD);
     add(&L.qkv, (Q + 2 * KV) * H);
     add(&L.o, H * Q);
-    add(&L.gu, 2 * I * H);
-    add(&L.down, H * I);
+    if (c->moe_experts > 0) {
+      const size_t E = size_t(c->moe_experts), MI = size_t(c->moe_inter);
+      add(&L.router, E * H);
+      if (allocate) {
+        L.egu.assign(E, nullptr);
+        L.edown.assign(E, nullptr);
+      }
+      for (size_t e = 0; e < E; ++e) {
+        add(&L.egu[e], 2 * MI * H);
+        add(&L.edown[e], H * MI);
+      }
+    } else {
+      add(&L.gu, 2 * I * H);
+      add(&L.down, H * I);
+    }
   }
   return out;
 }
 
 // Packed cache header: magic, packing layout version, the model description.
 constexpr char kPackedMagic[8] = {'M', 'M', 'C', 'P', 'K', '0', '0', '1'};
-constexpr uint32_t kPackedLayout = 1;  // rows fp16 RNE, norms folded, gate/up interleaved by 8
+constexpr uint32_t kPackedLayout = 2;  // rows fp16 RNE, norms folded, gate/up interleaved by 8, MoE fields
 
 // Upload all tensors; `get(i, staging)` fills host fp32 tensor i.
 template <typename Getter>
 void upload_weights(mmc_ctx* c, Getter&& get) {
   const auto& d = c->d;
   const int64_t H = d.hidden_size, V = d.vocab_size, Q = c->q_size(), KV = c->kv_size(), I = d.intermediate_size;
-  const int n = 3 + 11 * int(d.num_hidden_layers);
+  const int n = tensor_total(c);
   int64_t max_count = 0;
-  for (int i = 0; i < n; ++i) max_count = std::max(max_count, expected_count(d, i));
+  for (int i = 0; i < n; ++i) max_count = std::max(max_count, expected_count(c, i));
   float* stage_d = nullptr;
   ck(cudaMalloc(&stage_d, size_t(max_count) * 4 * 2), "weight staging");
   std::unique_ptr<float, void (*)(float*)> guard(stage_d, [](float* p) { cudaFree(p); });
@@ -776,7 +893,7 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
   c->layers.assign(size_t(d.num_hidden_layers), Layer{});
   for (int l = 0; l < int(d.num_hidden_layers); ++l) {
     Layer& L = c->layers[l];
-    const int base = 3 + 11 * l;
+    const int base = 3 + layer_tensors(c) * l;
     L.in_norm = c->alloc<float>(size_t(H), "norm");
     put(base + 0, L.in_norm);
     L.post_norm = c->alloc<float>(size_t(H), "norm");
@@ -800,15 +917,38 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
     put(base + 7, stage_d);
     ck(mmc::launch_pack_rows(stage_d, L.o, H, Q, c->stream), "pack o");
     ck(cudaStreamSynchronize(c->stream), "pack");
-    L.gu = c->alloc<__half>(size_t(2 * I * H), "gate_up");
-    put(base + 8, stage_d);
-    put(base + 9, stage_d2);
-    ck(mmc::launch_pack_gate_up(stage_d, stage_d2, L.gu, I, H, c->stream, L.post_norm), "pack gate_up");
-    ck(cudaStreamSynchronize(c->stream), "pack");
-    L.down = c->alloc<__half>(size_t(H * I), "down");
-    put(base + 10, stage_d);
-    ck(mmc::launch_pack_rows(stage_d, L.down, H, I, c->stream), "pack down");
-    ck(cudaStreamSynchronize(c->stream), "pack");
+    if (c->moe_experts > 0) {
+      // router rows and each expert's gate/up + down, packed like the dense MLP
+      // (the post-attention norm folded into the router and gate/up columns)
+      const int64_t E = c->moe_experts, MI = c->moe_inter;
+      L.router = c->alloc<__half>(size_t(E * H), "router");
+      put(base + 8, stage_d);
+      ck(mmc::launch_pack_rows(stage_d, L.router, E, H, c->stream, L.post_norm), "pack router");
+      ck(cudaStreamSynchronize(c->stream), "pack");
+      L.egu.assign(size_t(E), nullptr);
+      L.edown.assign(size_t(E), nullptr);
+      for (int64_t e = 0; e < E; ++e) {
+        L.egu[e] = c->alloc<__half>(size_t(2 * MI * H), "expert gate_up");
+        put(base + 9 + 3 * int(e), stage_d);
+        put(base + 10 + 3 * int(e), stage_d2);
+        ck(mmc::launch_pack_gate_up(stage_d, stage_d2, L.egu[e], MI, H, c->stream, L.post_norm), "pack expert");
+        ck(cudaStreamSynchronize(c->stream), "pack");
+        L.edown[e] = c->alloc<__half>(size_t(H * MI), "expert down");
+        put(base + 11 + 3 * int(e), stage_d);
+        ck(mmc::launch_pack_rows(stage_d, L.edown[e], H, MI, c->stream), "pack expert down");
+        ck(cudaStreamSynchronize(c->stream), "pack");
+      }
+    } else {
+      L.gu = c->alloc<__half>(size_t(2 * I * H), "gate_up");
+      put(base + 8, stage_d);
+      put(base + 9, stage_d2);
+      ck(mmc::launch_pack_gate_up(stage_d, stage_d2, L.gu, I, H, c->stream, L.post_norm), "pack gate_up");
+      ck(cudaStreamSynchronize(c->stream), "pack");
+      L.down = c->alloc<__half>(size_t(H * I), "down");
+      put(base + 10, stage_d);
+      ck(mmc::launch_pack_rows(stage_d, L.down, H, I, c->stream), "pack down");
+      ck(cudaStreamSynchronize(c->stream), "pack");
+    }
   }
   finish_load(c);
 }
@@ -909,11 +1049,11 @@ int mmc_load_weights(mmc_ctx* c, const float* const* tensors, const int64_t* cou
     require(c && tensors && counts, MMC_ERR_INVALID, "null argument");
     require(!c->loaded, MMC_ERR_STATE, "weights already loaded");
     use_device(c);
-    const int expect = 3 + 11 * int(c->d.num_hidden_layers);
+    const int expect = tensor_total(c);
     require(n == expect, MMC_ERR_INVALID, "expected " + std::to_string(expect) + " tensors in weights.bin order");
     for (int i = 0; i < n; ++i)
-      require(counts[i] == expected_count(c->d, i) && tensors[i], MMC_ERR_INVALID,
-              tensor_name(c->d, i) + " has invalid size");
+      require(counts[i] == expected_count(c, i) && tensors[i], MMC_ERR_INVALID,
+              tensor_name(c, i) + " has invalid size");
     upload_weights(c, [&](int i, std::vector<float>& h) { h.assign(tensors[i], tensors[i] + counts[i]); });
   });
 }
@@ -936,15 +1076,28 @@ int mmc_load_weights_file(mmc_ctx* c, const char* path) {
       require(bool(in) && len < 4096, MMC_ERR_IO, "failed to read tensor name");
       std::string name(len, '\0');
       in.read(name.data(), std::streamsize(len));
-      const std::string want = tensor_name(c->d, i);
+      const std::string want = tensor_name(c, i);
       require(bool(in) && name == want, MMC_ERR_IO, "expected tensor " + want + ", got " + name);
       uint64_t count = 0;
       in.read(reinterpret_cast<char*>(&count), 8);
-      require(bool(in) && int64_t(count) == expected_count(c->d, i), MMC_ERR_IO, want + " has invalid size");
+      require(bool(in) && int64_t(count) == expected_count(c, i), MMC_ERR_IO, want + " has invalid size");
       h.resize(count);
       in.read(reinterpret_cast<char*>(h.data()), std::streamsize(count * 4));
       require(bool(in), MMC_ERR_IO, "failed to read " + want);
     });
+  });
+}
+
+int mmc_configure_moe(mmc_ctx* c, int32_t num_experts, int64_t moe_intermediate_size) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    require(!c->loaded && !c->kv_ready, MMC_ERR_STATE, "configure MoE before loading weights and the KV cache");
+    require(num_experts >= 1 && num_experts <= 64, MMC_ERR_INVALID, "num_experts outside [1, 64]");
+    require(moe_intermediate_size > 0 && moe_intermediate_size % 64 == 0, MMC_ERR_INVALID,
+            "moe_intermediate_size must be a positive multiple of 64");
+    c->moe_experts = num_experts;
+    c->moe_inter = moe_intermediate_size;
+    c->mlp_chain = false;  // the projection chain covers the dense MLP only
   });
 }
 
@@ -960,6 +1113,8 @@ int mmc_save_packed(mmc_ctx* c, const char* path) {
       out.write(kPackedMagic, 8);
       out.write(reinterpret_cast<const char*>(&kPackedLayout), 4);
       out.write(reinterpret_cast<const char*>(&c->d), sizeof(mmc_model_desc));
+      const int64_t moe[2] = {c->moe_experts, c->moe_inter};
+      out.write(reinterpret_cast<const char*>(moe), sizeof(moe));
       std::vector<char> host;
       for (auto& [slot, bytes] : packed_buffers(c, false)) {
         host.resize(bytes);
@@ -987,9 +1142,12 @@ int mmc_load_packed(mmc_ctx* c, const char* path) {
     in.read(magic, 8);
     in.read(reinterpret_cast<char*>(&layout), 4);
     in.read(reinterpret_cast<char*>(&d), sizeof(d));
+    int64_t moe[2] = {0, 0};
+    in.read(reinterpret_cast<char*>(moe), sizeof(moe));
     require(bool(in) && std::memcmp(magic, kPackedMagic, 8) == 0 && layout == kPackedLayout, MMC_ERR_IO,
             "not a packed weight cache of this library version");
-    require(std::memcmp(&d, &c->d, sizeof(d)) == 0, MMC_ERR_INVALID, "packed weights were made for another model");
+    require(std::memcmp(&d, &c->d, sizeof(d)) == 0 && moe[0] == c->moe_experts && moe[1] == c->moe_inter,
+            MMC_ERR_INVALID, "packed weights were made for another model");
     // read everything before allocating, so a short file leaves the context unloaded
     c->layers.assign(size_t(c->d.num_hidden_layers), Layer{});
     auto slots = packed_buffers(c, false);  // sizes only (pointers not yet allocated)
@@ -1043,10 +1201,12 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->hidden = c->alloc<float>(size_t(max_batch) * H, "hidden");
     c->qkv = c->alloc<float>(size_t(max_batch) * (Q + 2 * KV), "qkv");
     c->attn = c->alloc<float>(size_t(max_batch) * Q, "attn");
-    c->act = c->alloc<float>(size_t(max_batch) * I, "act");
+    const int64_t IA = std::max<int64_t>(I, c->moe_inter);  // MLP activation width (dense or expert)
+    c->act = c->alloc<float>(size_t(max_batch) * IA, "act");
+    c->expert_ids = c->alloc<int>(size_t(max_batch), "routed experts");
     c->h16 = c->alloc<__half>(size_t(max_batch) * H, "residual rows fp16");
     c->attn16 = c->alloc<__half>(size_t(max_batch) * Q, "attention output fp16");
-    c->act16 = c->alloc<__half>(size_t(max_batch) * I, "act fp16");
+    c->act16 = c->alloc<__half>(size_t(max_batch) * IA, "act fp16");
     c->q16 = c->alloc<__half>(size_t(max_batch) * Q, "q fp16");
     c->logits = c->alloc<float>(size_t(max_batch) * V, "logits");
     c->tokens = c->alloc<int>(size_t(max_batch), "tokens");

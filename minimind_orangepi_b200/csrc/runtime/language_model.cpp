@@ -68,6 +68,10 @@ class DeviceModel {
     const mmc_model_desc d = describe(config);
     mmc_check(mmc_create(&d, o.device, &ctx_));
     try {
+      if (config.use_moe) {
+        if (weights != nullptr) throw std::invalid_argument("MoE models load on the device from weights.bin");
+        mmc_check(mmc_configure_moe(ctx_, static_cast<int32_t>(config.num_experts), config.moe_intermediate_size));
+      }
       if (weights != nullptr) {
         std::vector<const float*> ptrs;
         std::vector<int64_t> counts;
@@ -148,7 +152,6 @@ LanguageModel::LanguageModel(MiniMindConfig config, std::string weights_bin, Run
 
 DeviceModel& LanguageModel::device() const {
   if (!device_) {
-    if (config_.use_moe) throw std::invalid_argument("the CUDA decode path supports dense models only");
     device_ = std::make_shared<DeviceModel>(config_, weights_bin_.empty() ? &weights_ : nullptr, weights_bin_,
                                             options_);
     if (weights_bin_.empty()) {

@@ -31,6 +31,8 @@ class RuntimeConfig:
     intermediate_size: int = 2432
     max_position_embeddings: int = 32768
     tie_word_embeddings: bool = True
+    num_experts: int = 4
+    moe_intermediate_size: int = 0  # 0: intermediate_size
     rms_norm_eps: float = DEFAULT_EPS
     rope_theta: float = DEFAULT_THETA
     bos_token_id: int = 1
@@ -63,6 +65,8 @@ def read_runtime_config(model_dir) -> RuntimeConfig:
     c.intermediate_size = gi("intermediate_size", c.intermediate_size)
     c.max_position_embeddings = gi("max_position_embeddings", c.max_position_embeddings)
     c.tie_word_embeddings = gb("tie_word_embeddings", c.tie_word_embeddings)
+    c.num_experts = gi("num_experts", c.num_experts)
+    c.moe_intermediate_size = gi("moe_intermediate_size", c.intermediate_size)
     if "rms_norm_eps" in values:
         c.rms_norm_eps = float(values["rms_norm_eps"])
     if "rope_theta" in values:
@@ -80,8 +84,6 @@ class DecodeEngine:
                  pages_budget_tokens: int | None = None, packed_cache=None):
         self.L = lib()
         self.config = read_runtime_config(model_dir)
-        if self.config.use_moe:
-            raise ValueError("MoE checkpoints are not supported by the CUDA decode path")
         c = self.config
         d = ModelDesc(c.hidden_size, c.num_hidden_layers, c.num_attention_heads, c.num_key_value_heads, c.head_dim,
                       c.intermediate_size, c.vocab_size, c.max_position_embeddings,
@@ -91,6 +93,8 @@ class DecodeEngine:
         self.h = h
         self.device = device
         try:
+            if c.use_moe:  # top-1 MoE MLP (decoder_layer.cpp:370-389)
+                check(self.L.mmc_configure_moe(self.h, c.num_experts, c.moe_intermediate_size))
             self.loaded_from = self._load(Path(model_dir), packed_cache)
             if n_pages is None:
                 tokens = pages_budget_tokens or max_seqs * 2048

@@ -55,6 +55,10 @@ typedef struct {
 } mmo_state;
 
 static char g_err[256];
+/* smallest router top-2 margin (top1 - top2, relative to |top1|) over the
+ * layers of the last mmo_forward_token call; INFINITY for dense models */
+static float g_router_margin = INFINITY;
+MMO_API float mmo_last_router_margin(void) { return g_router_margin; }
 MMO_API const char *mmo_last_error(void) { return g_err; }
 
 /* ---------------------------------------------------------------- kernels */
@@ -393,6 +397,11 @@ static void decoder_layer(const mmo_model *m, const mmo_layer *L, mmo_cache *cac
     float *router = (float *)malloc((size_t)c->experts * sizeof(float));
     mmo_matvec(L->moe_gate, c->experts, H, normed, router);
     const int64_t e = mmo_argmax(router, c->experts);
+    float second = -INFINITY;
+    for (int64_t k = 0; k < c->experts; ++k)
+      if (k != e && router[k] > second) second = router[k];
+    const float margin = (router[e] - second) / (fabsf(router[e]) + 1e-12f);
+    if (margin < g_router_margin) g_router_margin = margin;
     free(router);
     const int64_t MI = c->moe_inter;
     mmo_matvec(L->exp_gate_up[e], 2 * MI, H, normed, gu);
@@ -418,6 +427,7 @@ MMO_API int32_t mmo_forward_token(const mmo_model *m, mmo_state *s, int32_t toke
     return -1;
   }
   float *hidden = (float *)malloc((size_t)c->hidden * sizeof(float));
+  g_router_margin = INFINITY;
   memcpy(hidden, m->embed + (int64_t)token * c->hidden, (size_t)c->hidden * sizeof(float));
   for (int64_t l = 0; l < c->layers; ++l) decoder_layer(m, &m->layer[l], &s->cache[l], hidden, s->position);
   s->position += 1;

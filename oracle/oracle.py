@@ -52,6 +52,7 @@ def lib() -> C.CDLL:
         L.mmo_generate.argtypes = [P, C.POINTER(I32), I64, I64, I32, C.POINTER(I32)]
         L.mmo_config_of.argtypes = [P, C.POINTER(MmoConfig)]
         L.mmo_last_error.restype = C.c_char_p
+        L.mmo_last_router_margin.restype = C.c_float
         L.mmo_matvec.argtypes = [F, I64, I64, F, F]
         L.mmo_rms_norm_inplace.argtypes = [F, F, I64, C.c_float]
         L.mmo_rms_norm_final.argtypes = [F, F, I64, C.c_float, F]
@@ -99,6 +100,13 @@ class Oracle:
         if nxt < 0:
             raise IndexError(self.L.mmo_last_error().decode())
         return nxt, logits
+
+    def router_margin(self) -> float:
+        """Smallest top-1 vs top-2 router margin (relative to |top-1|) over the
+        layers of the last forward_token; inf for dense models. A small margin
+        means an implementation with fp16 weights may route that token to the
+        other expert."""
+        return float(self.L.mmo_last_router_margin())
 
     def generate(self, prompt, max_new: int, eos: int = 2):
         p = (C.c_int32 * len(prompt))(*prompt)

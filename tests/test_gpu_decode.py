@@ -24,6 +24,7 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden"
 ATOL, RTOL = 2e-2, 1e-2
+ROUTER_MARGIN = 1e-2  # relative top-1 vs top-2 router margin below which an fp16 path may pick the other expert
 
 
 def close(a, b):
@@ -40,7 +41,7 @@ def check_step(logits, ref_logits, ref_next, got_next, where):
     assert got_next == int(np.argmax(logits)), f"{where}: argmax not the first maximum of the kernel's logits"
 
 
-@pytest.mark.parametrize("name", ["tiny", "tiny-hd64", "tiny-hd96-page-cross", "cfg1-minimind2-small"])
+@pytest.mark.parametrize("name", ["tiny", "tiny-hd64", "tiny-hd96-page-cross", "cfg1-minimind2-small", "tiny-moe"])
 def test_decode_matches_reference_golden(name, tmp_path_factory):
     g = np.load(GOLDEN / f"{name}.npz")
     shape = ModelShape(**json.loads(str(g["shape"])))
@@ -105,7 +106,8 @@ def test_decode_matches_live_oracle(shape, plen, steps, model_dir):
             assert k.shape[0] == plen + steps - 1
 
 
-@pytest.mark.parametrize("shape,batch,steps", [("tiny-hd64", 3, 30), ("tiny-hd64", 37, 24),
+@pytest.mark.parametrize("shape,batch,steps", [("tiny-moe", 3, 20), ("tiny-moe", 37, 16), ("tiny-moe", 140, 4),
+                                              ("tiny-hd64", 3, 30), ("tiny-hd64", 37, 24),
                                                ("minimind2-small", 8, 12), ("tiny-hd96", 70, 12)])
 def test_batched_decode_matches_oracle(shape, batch, steps, model_dir):
     """Independent sequences with different prompt lengths decode together;
@@ -119,6 +121,8 @@ def test_batched_decode_matches_oracle(shape, batch, steps, model_dir):
     plens = [int(x) for x in rng.integers(1, 90, size=batch)]
     prompts = [synthetic_prompt(100 + i, n, vocab=s.vocab_size) for i, n in enumerate(plens)]
     states = [orc.new_state() for _ in range(batch)]
+    diverged: set[int] = set()
+    checked = total = 0
     with DecodeEngine(d, max_seqs=batch + 4, max_batch=batch) as eng:
         seqs = [eng.open_sequence(plens[i] + steps + 1) for i in range(batch)]
         cur = [p[0] for p in prompts]
@@ -130,14 +134,23 @@ def test_batched_decode_matches_oracle(shape, batch, steps, model_dir):
             nxt, logits = eng.step([seqs[i] for i in rows], [cur[i] for i in rows], want_logits=True)
             for j, i in enumerate(rows):
                 ref_next, ref_logits = orc.forward_token(states[i], cur[i])
-                check_step(logits[j], ref_logits, ref_next, int(nxt[j]), f"{shape} B={batch} row {i} step {fed[i]}")
+                # MoE: once the reference's router top-2 margin is this small, fp16
+                # rounding may route the token to the other expert and the sequence
+                # legitimately diverges; it is compared up to that point only
+                if orc.router_margin() < ROUTER_MARGIN:
+                    diverged.add(i)
+                total += 1
+                if i not in diverged:
+                    checked += 1
+                    check_step(logits[j], ref_logits, ref_next, int(nxt[j]), f"{shape} B={batch} row {i} step {fed[i]}")
                 fed[i] += 1
                 cur[i] = prompts[i][fed[i]] if fed[i] < plens[i] else ref_next
         for i in range(batch):
             assert eng.position(seqs[i]) == fed[i]
+        assert checked >= 0.5 * total, f"only {checked} of {total} steps compared (router near-ties)"
 
 
-@pytest.mark.parametrize("shape,batch", [("minimind2-small", 1), ("tiny-hd96", 16)])
+@pytest.mark.parametrize("shape,batch", [("minimind2-small", 1), ("tiny-hd96", 16), ("tiny-moe", 16)])
 def test_graph_loop_matches_stepwise(shape, batch, model_dir):
     """The captured device-resident loop produces the same tokens as eager steps."""
     d = model_dir(shape, seed=3)
@@ -182,3 +195,28 @@ def test_errors_are_reported(model_dir):
         eng.reserve(seq, 65)
         nxt, _ = eng.step([seq], [1])
         assert 0 <= int(nxt[0]) < 256
+
+
+def test_configure_moe_validation():
+    """mmc_configure_moe: only before loading, sane sizes only."""
+    import ctypes as C
+
+    from minimind_orangepi_b200._lib import lib
+    from minimind_orangepi_b200.engine import ModelDesc
+
+    s = SHAPES["tiny-moe"]
+    desc = ModelDesc(s.hidden_size, s.num_hidden_layers, s.num_attention_heads, s.num_key_value_heads, s.head_dim,
+                     s.intermediate_size, s.vocab_size, s.max_position_embeddings, 1e-5, 1e6)
+    h = C.c_void_p()
+    assert lib().mmc_create(C.byref(desc), 0, C.byref(h)) == 0
+    try:
+        assert lib().mmc_configure_moe(h, 0, 256) == 1  # MMC_ERR_INVALID
+        assert lib().mmc_configure_moe(h, 4, 100) == 1  # not a multiple of 64
+        d = write_runtime_model(Path("/tmp/mmc_test_models") / "cfg-tiny-moe", "tiny-moe", 2, eps=1e-5, theta=1e6)
+        # a dense context cannot read a MoE weights.bin (tensor names differ)
+        assert lib().mmc_load_weights_file(h, str(d / "weights.bin").encode()) != 0
+        assert lib().mmc_configure_moe(h, 4, 256) == 0
+        assert lib().mmc_load_weights_file(h, str(d / "weights.bin").encode()) == 0
+        assert lib().mmc_configure_moe(h, 4, 256) == 6  # MMC_ERR_STATE after loading
+    finally:
+        lib().mmc_destroy(h)

@@ -40,7 +40,7 @@ def golden_model(name):
 
 
 @pytest.mark.parametrize("name,max_batch", [("tiny-hd96-page-cross", 128), ("tiny-hd96-page-cross", 16),
-                                            ("tiny-hd64", 64), ("cfg1-minimind2-small", 8)])
+                                            ("tiny-hd64", 64), ("cfg1-minimind2-small", 8), ("tiny-moe", 16)])
 def test_prompt_pass_matches_reference_golden(name, max_batch):
     """Prompt = the fixture's first n fed tokens through mmc_prefill (in passes
     of max_batch rows), then the remaining fed tokens by decode steps: every
