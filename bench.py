@@ -43,6 +43,10 @@ WORKLOADS = {
                  desc="BASELINE config 4: batched decode, MiniMind2 (768 hidden, 16 layers, 8q/2kv, hd 96, "
                       "inter 2048, vocab 6400), 256 sequences, prompt lengths U[16,2048], 256 greedy steps, "
                       "paged fp16 KV"),
+    "cfg4-shard8": dict(shape="minimind2", n_seqs=32, prompt=(16, 2048), steps=64,
+                        desc="one GPU's share of BASELINE config 4 on 8 GPUs (32 sequences; profiling case)"),
+    "cfg4-shard4": dict(shape="minimind2", n_seqs=64, prompt=(16, 2048), steps=64,
+                        desc="one GPU's share of BASELINE config 4 on 4 GPUs (64 sequences; profiling case)"),
     "probe": dict(shape="minimind2", n_seqs=96, prompt=(16, 512), steps=8,
                   desc="profiling case (not a BASELINE config): MiniMind2, 96 sequences, prompt lengths U[16,512]"),
     "cfg3": dict(shape="minimind2", n_seqs=1, prompt=(128, 128), steps=1024,

@@ -489,8 +489,9 @@ int split_plan(const TcArgs& a, int epi, int* bn) {
   if (!enabled || epi == kEpiArgmax || a.max_splits < 2) return 1;
   const int mt = (a.N + UM - 1) / UM, KT = a.K / BK;
   if (mt * ((a.B + *bn - 1) / *bn) >= target || KT < 4) return 1;
+  const int cap = a.split_bn > 0 ? a.split_bn : bn_cap;
   int b = 16;
-  while (b < bn_cap && b < a.B) b *= 2;
+  while (b < cap && b < a.B) b *= 2;
   const int tiles = mt * ((a.B + b - 1) / b);
   const int S = std::min(std::min(KT / 2, std::min(a.max_splits, 8)), (target + tiles - 1) / tiles);
   if (S < 2) return 1;

@@ -100,6 +100,7 @@ struct TcArgs {
   // and reduce their accumulators over distributed shared memory (fixed order)
   int splits = 1;      // set by the launcher
   int max_splits = 8;  // caller's cap (1: never split)
+  int split_bn = 0;    // batch tile when splitting (0: the planner's default)
   // RMSNorm folded across kernels (the norm weight is folded into W's
   // columns at load time): a consumer with ss_in scales its outputs by
   // rs[b] = 1 / sqrt(sum_m ss_in[b][m] / K + eps), m < ceil(K / 128); a

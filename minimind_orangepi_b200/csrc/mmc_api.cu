@@ -137,6 +137,7 @@ struct mmc_ctx {
   unsigned* attn_counters = nullptr;
   unsigned* attn_work = nullptr;  // [parts][4] attention work-queue words
   int decode_split_k = env_int("MMC_DECODE_SPLIT_K", 1);
+  int decode_split_k_alone = env_int("MMC_DECODE_SPLIT_K_ALONE", 4);
   unsigned* chain_sync = nullptr;  // [parts][chain_sync_words(max_batch)] projection-chain queues
   int chain_words = 0;
   bool mlp_chain = false;  // MMC_MLP_CHAIN at creation
@@ -243,6 +244,7 @@ struct StepIO {
   int64_t total_pages = 1, max_ctx = 1;  // attention plan inputs (whole batch)
   int attn_ctas_per_sm = 2;  // persistent attention CTAs per SM (1 when concurrent batch parts share the GPU)
   const int* row_off = nullptr;  // prompt pass: per-row position offsets (positions advanced by the host)
+  bool alone = true;  // the batch runs as one part (nothing concurrent competes for the SMs)
   int row0 = 0;  // first scratch row of this part of the batch
   int part = 0;  // 0 .. kMaxParts-1: which counter region this part uses
 };
@@ -343,9 +345,13 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     mmc::TcArgs t;
     t.row_sel = row_sel;
     t.row_sel_val = row_sel_val;
-    // split-K clusters lose to plain tiles inside the decode step (measured on
-    // B200 with concurrent batch parts); MMC_DECODE_SPLIT_K=n allows n
-    t.max_splits = c->decode_split_k;
+    // Split-K (thread-block clusters) spreads a projection's weight tiles over
+    // more SMs. Measured on B200: it wins for a batch that runs alone (few CTAs
+    // per projection: 0.99 -> 0.87 ms/step at 32 sequences) and loses when
+    // concurrent batch parts already fill the GPU. MMC_DECODE_SPLIT_K /
+    // MMC_DECODE_SPLIT_K_ALONE cap the splits for the two cases.
+    t.max_splits = io.alone ? c->decode_split_k_alone : c->decode_split_k;
+    t.split_bn = 16;
     if (normed) {
       t.ss_in = ss;
       t.eps = d.rms_norm_eps;
@@ -666,6 +672,7 @@ void enqueue_batch(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
     a.B = n;
     a.row0 = io.row0 + r0;
     a.part = i;
+    a.alone = false;
     a.slots = io.slots + r0;
     if (io.row_off) a.row_off = io.row_off + r0;
     a.tokens = io.tokens + r0;
