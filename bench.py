@@ -45,6 +45,8 @@ WORKLOADS = {
                       "paged fp16 KV"),
     "cfg4-shard8": dict(shape="minimind2", n_seqs=32, prompt=(16, 2048), steps=64,
                         desc="one GPU's share of BASELINE config 4 on 8 GPUs (32 sequences; profiling case)"),
+    "cfg4-shard2": dict(shape="minimind2", n_seqs=128, prompt=(16, 2048), steps=64,
+                        desc="one GPU's share of BASELINE config 4 on 2 GPUs (128 sequences; profiling case)"),
     "cfg4-shard4": dict(shape="minimind2", n_seqs=64, prompt=(16, 2048), steps=64,
                         desc="one GPU's share of BASELINE config 4 on 4 GPUs (64 sequences; profiling case)"),
     "probe": dict(shape="minimind2", n_seqs=96, prompt=(16, 512), steps=8,
