@@ -205,8 +205,9 @@ MMC_EXPORT int mmc_graph_tokens(mmc_ctx* ctx, int32_t n_steps, int32_t* tokens_h
 
 /* Wait for the context's stream and report any device-side error. */
 MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
-/* Number of kernels one decode step launches for a batch of `batch` rows
- * (6 per layer + 1 for batch <= 4, 8 per layer + 2 above). */
+/* Number of kernels one decode step launches for a batch of `batch` rows:
+ * 6 per layer + 1 for batch <= 4; above, 6 per layer + 2 for each of the
+ * concurrent parts the batch runs as (up to 4 parts of >= 64 rows). */
 MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* kernels);
 
 /* ------------------------------------------------------------- single ops
@@ -244,15 +245,30 @@ MMC_EXPORT int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t 
                      const int32_t* d_block_table, int32_t max_pages, const int32_t* d_seq_pos,
                      const int32_t* d_slots, int32_t max_ctx, float* d_out, void* d_workspace,
                      size_t workspace_bytes, void* stream);
+/* Reports a device-side error of the last mmc_op_attention launched with the
+ * workspace `d_workspace` on `stream`: waits for the stream, reads the
+ * kernel's error word (the first int of the workspace) and returns
+ * MMC_ERR_DEVICE with the reason (KV position without a page in the block
+ * table, position past max_pos, a bounded wait that ran out) if it is set,
+ * clearing it. mmc_op_attention itself stays asynchronous and does not read
+ * it. Replaces the error checks after aclnn launches (check_acl,
+ * ascend_custom_ops.cpp:875-883). */
+MMC_EXPORT int mmc_op_attention_status(const void* d_workspace, void* stream);
 /* mmc_op_attention without a workspace argument, for callers that cannot
- * allocate device memory (no cudaMalloc where they run: allocator hooks, host
- * callbacks, hosts that own all device memory). No counterpart in the
- * reference. The scratch is a fixed 16 MiB array inside the library that every
- * GPU loading it keeps until exit; sizes needing more scratch than that (see
- * mmc_op_attention_workspace_size) fail with MMC_ERR_INVALID. The first call on
- * a device looks up the array's address with that device current (make it
- * before any stream capture). The array is shared by all calls: calls that
- * overlap on the GPU race. Allocates nothing. */
+ * allocate device memory where they run (a custom allocator's own hooks, a
+ * loop with a no-allocation rule, hosts that own all device memory). No
+ * counterpart in the reference. The scratch is a fixed 16 MiB array inside the
+ * library that every GPU loading it keeps until exit; sizes needing more
+ * scratch than that (see mmc_op_attention_workspace_size) fail with
+ * MMC_ERR_INVALID. The first call on a device looks up the array's address
+ * with that device current (make it before any stream capture); with lazy
+ * module loading that first call may also allocate the array's backing, so
+ * warm up once (or set CUDA_MODULE_LOADING=EAGER) before a region where
+ * allocation is forbidden. The cached address belongs to the device's primary
+ * context: do not call after cudaDeviceReset. The array is shared by all
+ * calls: calls that overlap on the GPU race. The call waits for its kernel and
+ * returns MMC_ERR_DEVICE if the kernel reported an error. Allocates nothing
+ * after the first call. */
 MMC_EXPORT int mmc_op_attention_noalloc(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t layer,
                                         int32_t layers, const float* d_qkv, const float* d_q_norm,
                                         const float* d_k_norm, const float* d_rope_cos, const float* d_rope_sin,

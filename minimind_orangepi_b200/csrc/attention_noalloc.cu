@@ -2,11 +2,19 @@
 //
 // mmc_op_attention needs a caller-provided workspace (split partials, arrival
 // counters, an error word). Some callers cannot provide one: code that runs
-// where cudaMalloc is forbidden or unsafe (inside a host callback, a custom
-// allocator's own hooks, a real-time loop with a no-allocation rule, or a
-// plugin host that owns all device memory). For them this file keeps a fixed
-// workspace in a file-scope __device__ array that every GPU loading the
-// library holds until the process exits, and passes it to the same kernel.
+// where cudaMalloc is forbidden or unsafe (a custom allocator's own hooks, a
+// real-time loop with a no-allocation rule, or a plugin host that owns all
+// device memory). For them this file keeps a fixed workspace in a file-scope
+// __device__ array that every GPU loading the library holds until the process
+// exits, and passes it to the same kernel.
+//
+// The array's address is looked up once per device and cached for the life of
+// the process; it belongs to that device's primary context, so the entry point
+// must not be used after cudaDeviceReset (or from a non-primary context).
+// With lazy module loading (the CUDA 12 default) the first call on a device
+// loads the module, which may allocate the array's backing memory: make one
+// warm-up call, or run with CUDA_MODULE_LOADING=EAGER, before entering a
+// region where allocation is forbidden.
 #include "../../include/minimind_cuda.h"
 
 #include <cuda_runtime.h>
@@ -68,7 +76,12 @@ extern "C" int mmc_op_attention_noalloc(int32_t batch, int32_t nq, int32_t nkv, 
   // mmc_op_attention zeroes the counters and error word of its workspace on
   // `stream` before the launch, so stale contents from an earlier call are
   // harmless. Calls that overlap on the GPU share this array and race.
-  return mmc_op_attention(batch, nq, nkv, hd, layer, layers, d_qkv, d_q_norm, d_k_norm, d_rope_cos, d_rope_sin, max_pos,
+  rc = mmc_op_attention(batch, nq, nkv, hd, layer, layers, d_qkv, d_q_norm, d_k_norm, d_rope_cos, d_rope_sin, max_pos,
                         eps, d_kv_pool, d_block_table, max_pages, d_seq_pos, d_slots, max_ctx, d_out, scratch,
-                          kNoAllocScratchBytes, stream);
+                        kNoAllocScratchBytes, stream);
+  if (rc != MMC_OK) return rc;
+  // The caller cannot see the error word inside this library's array, so the
+  // call waits for the kernel and reports a device-side error (a missing KV
+  // page, a position past max_pos, a bounded wait that ran out) itself.
+  return mmc_op_attention_status(scratch, stream);
 }

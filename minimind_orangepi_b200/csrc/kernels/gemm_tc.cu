@@ -320,11 +320,12 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
   if (EPI != kEpiArgmax) return;
 
   ArgBest* part = reinterpret_cast<ArgBest*>(a.argmax_part);
-  if (tid < BN && n0 + tid < a.B) {
+  // every batch column of the tile (BN may exceed the thread count)
+  for (int c = tid; c < BN && n0 + c < a.B; c += kThreads) {
     ArgBest bb = {-INFINITY, 0x7fffffff};
     for (int w = 0; w < 4; ++w)
-      if (better(best_s[w][tid].v, best_s[w][tid].i, bb.v, bb.i)) bb = best_s[w][tid];
-    part[size_t(n0 + tid) * gridDim.x + blockIdx.x] = bb;
+      if (better(best_s[w][c].v, best_s[w][c].i, bb.v, bb.i)) bb = best_s[w][c];
+    part[size_t(n0 + c) * gridDim.x + blockIdx.x] = bb;
   }
   __threadfence();
   __syncthreads();

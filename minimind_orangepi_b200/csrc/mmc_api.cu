@@ -2,7 +2,7 @@
 // behind the C ABI declared in include/minimind_cuda.h.
 //
 // One decode step for B rows is a fixed chain of kernels on one stream
-// (6 per layer + 1; 8 + 2 on the tensor-core path), every launch after the first carrying programmatic
+// (6 per layer + 1; 6 per layer + 2 on the tensor-core path), every launch after the first carrying programmatic
 // stream serialization so each kernel's weight / KV-page prefetch overlaps its
 // predecessor:
 //   per layer: qkv projection (RMSNorm prologue; layer 0 gathers the embedding)
@@ -13,7 +13,7 @@
 //   lm_head projection (final RMSNorm prologue, argmax epilogue; writes the
 //   next tokens back into the token buffer and advances the positions)
 // B <= 4 uses the CUDA-core projections (gemv.cu), larger batches the
-// tensor-core ones (gemm_mma.cu). The chain can be captured once as a CUDA
+// tensor-core ones (gemm_tc.cu). The chain can be captured once as a CUDA
 // graph and replayed with the tokens fed back on the device.
 #include "../../include/minimind_cuda.h"
 #include "kernels/kernels.h"
@@ -185,18 +185,21 @@ void require(bool ok, int code, const std::string& msg) {
   if (!ok) fail(code, msg);
 }
 
+const char* device_error_text(int e) {
+  return e == mmc::kDevWaitTimeout     ? "a bounded wait timed out"
+         : e == mmc::kDevBadToken      ? "token id out of vocabulary range"
+         : e == mmc::kDevNoPage        ? "KV position not backed by a reserved page"
+         : e == mmc::kDevPositionLimit ? "position exceeds max_position_embeddings"
+                                       : "unknown";
+}
+
 // Raises MMC_ERR_DEVICE (and clears the word) if the device error word `e`,
 // already read back, is set.
 void raise_device_error(mmc_ctx* c, int e) {
   if (e != 0) {
     ck(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream), "clear device error word");
     ck(cudaStreamSynchronize(c->stream), "clear device error word");
-    const char* what = e == mmc::kDevWaitTimeout   ? "a bounded wait timed out"
-                       : e == mmc::kDevBadToken    ? "token id out of vocabulary range"
-                       : e == mmc::kDevNoPage      ? "KV position not backed by a reserved page"
-                       : e == mmc::kDevPositionLimit ? "position exceeds max_position_embeddings"
-                                                     : "unknown";
-    fail(MMC_ERR_DEVICE, std::string("device error: ") + what);
+    fail(MMC_ERR_DEVICE, std::string("device error: ") + device_error_text(e));
   }
 }
 
@@ -1684,13 +1687,24 @@ int mmc_synchronize(mmc_ctx* c) {
 int mmc_kernels_per_step(const mmc_ctx* c, int32_t batch, int32_t* k) {
   return guarded([&] {
     require(c && k, MMC_ERR_INVALID, "null argument");
-    *k = kernels_per_step(c, batch);
+    require(batch >= 1, MMC_ERR_INVALID, "bad batch");
+    // a batch that runs as concurrent parts launches each part's chain
+    const int P = batch > kGemvMaxBatch ? batch_parts(c, batch) : 1;
+    int total = 0;
+    for (int i = 0; i < P; ++i) {
+      int r0 = 0, n = batch;
+      if (P > 1) part_rows(batch, P, i, &r0, &n);
+      total += kernels_per_step(c, n);
+    }
+    *k = total;
   });
 }
 
 // ------------------------------------------------------------- single ops
 
 namespace {
+// first bytes of an attention-op workspace: error word at 0, work queue at 16
+constexpr size_t kOpAttnHeader = 256;
 void op_init_attributes() {
   static thread_local int done_dev = -1;
   int dev = 0;
@@ -1804,9 +1818,10 @@ int mmc_op_attention_workspace_size(int32_t batch, int32_t nq, int32_t nkv, int3
     require(batch >= 1 && nkv >= 1 && nq % nkv == 0 && hd > 0 && max_ctx >= 1 && bytes, MMC_ERR_INVALID,
             "bad arguments");
     const int splits = std::min(64, (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens);
-    // split partials | counters, error word, work queue | q heads (fp16)
-    *bytes = (mmc::attn_part_floats(batch, nkv, splits, nq / nkv, hd) * 4 + 255) / 256 * 256 +
-             (size_t(batch) * nkv * 4 + 32 + 255) / 256 * 256 + size_t(batch) * nq * hd * 2;
+    // header (error word, work queue) | arrival counters | split partials | q heads (fp16)
+    *bytes = kOpAttnHeader + (size_t(batch) * nkv * 4 + 255) / 256 * 256 +
+             (mmc::attn_part_floats(batch, nkv, splits, nq / nkv, hd) * 4 + 255) / 256 * 256 +
+             size_t(batch) * nq * hd * 2;
   });
 }
 
@@ -1849,17 +1864,34 @@ int mmc_op_attention(int32_t batch, int32_t nq, int32_t nkv, int32_t hd, int32_t
     a.max_splits = max_splits;
     a.out = out;
     uint8_t* base = static_cast<uint8_t*>(ws);
-    // workspace layout as sized by mmc_op_attention_workspace_size
+    // workspace layout as sized by mmc_op_attention_workspace_size; the error
+    // word is the first int, where mmc_op_attention_status reads it
     const int splits_ws = int(std::min<int64_t>(64, pages));
+    const size_t cbytes = (size_t(batch) * nkv * 4 + 255) / 256 * 256;
     const size_t pbytes = (mmc::attn_part_floats(batch, nkv, splits_ws, nq / nkv, hd) * 4 + 255) / 256 * 256;
-    a.part = reinterpret_cast<float*>(base);
-    a.counters = reinterpret_cast<unsigned*>(base + pbytes);
-    a.err = reinterpret_cast<int*>(base + pbytes + size_t(batch) * nkv * 4);
-    a.work = reinterpret_cast<unsigned*>(base + pbytes + size_t(batch) * nkv * 4 + 16);
-    a.q16 = reinterpret_cast<__half*>(base + pbytes + (size_t(batch) * nkv * 4 + 32 + 255) / 256 * 256);
+    a.err = reinterpret_cast<int*>(base);
+    a.work = reinterpret_cast<unsigned*>(base + 16);
+    a.counters = reinterpret_cast<unsigned*>(base + kOpAttnHeader);
+    a.part = reinterpret_cast<float*>(base + kOpAttnHeader + cbytes);
+    a.q16 = reinterpret_cast<__half*>(base + kOpAttnHeader + cbytes + pbytes);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    ck(cudaMemsetAsync(base + pbytes, 0, size_t(batch) * nkv * 4 + 32, s), "counter reset");
+    ck(cudaMemsetAsync(base, 0, kOpAttnHeader + size_t(batch) * nkv * 4, s), "counter reset");
     ck(mmc::launch_attention(a, s, false), "attention launch");
+  });
+}
+
+int mmc_op_attention_status(const void* ws, void* stream) {
+  return guarded([&] {
+    require(ws != nullptr, MMC_ERR_INVALID, "null workspace");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int e = 0;
+    ck(cudaMemcpyAsync(&e, ws, sizeof(int), cudaMemcpyDeviceToHost, s), "read attention error word");
+    ck(cudaStreamSynchronize(s), "read attention error word");
+    if (e != 0) {
+      ck(cudaMemsetAsync(const_cast<void*>(ws), 0, sizeof(int), s), "clear attention error word");
+      ck(cudaStreamSynchronize(s), "clear attention error word");
+      fail(MMC_ERR_DEVICE, std::string("device error: ") + device_error_text(e));
+    }
   });
 }
 

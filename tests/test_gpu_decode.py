@@ -41,7 +41,8 @@ def check_step(logits, ref_logits, ref_next, got_next, where):
     assert got_next == int(np.argmax(logits)), f"{where}: argmax not the first maximum of the kernel's logits"
 
 
-@pytest.mark.parametrize("name", ["tiny", "tiny-hd64", "tiny-hd96-page-cross", "cfg1-minimind2-small", "tiny-moe"])
+@pytest.mark.parametrize("name", ["tiny", "tiny-hd64", "tiny-hd96-page-cross", "cfg1-minimind2-small", "tiny-moe",
+                                  "cfg2-minimind2-small-long", "cfg3-minimind2"])
 def test_decode_matches_reference_golden(name, tmp_path_factory):
     g = np.load(GOLDEN / f"{name}.npz")
     shape = ModelShape(**json.loads(str(g["shape"])))

@@ -1,11 +1,12 @@
 """The allocation-free attention entry point (mmc_op_attention_noalloc).
 
-It exists for callers that may not call cudaMalloc where they run (allocator
-hooks, host callbacks, hosts that own all device memory): instead of a
-caller-provided workspace it uses a fixed scratch array inside the library.
-These tests call it through the C ABI twice in a row and compare each result
-with the workspace-taking mmc_op_attention on identical inputs, and check that
-a size beyond the fixed scratch is refused. This file is collected last on
+It exists for callers that may not call cudaMalloc where they run (a custom
+allocator's own hooks, loops with a no-allocation rule, hosts that own all
+device memory): instead of a caller-provided workspace it uses a fixed scratch
+array inside the library. These tests call it through the C ABI twice in a row
+and compare each result with the workspace-taking mmc_op_attention on identical
+inputs, check that a size beyond the fixed scratch is refused, and that a
+device-side error comes back as MMC_ERR_DEVICE. This file is collected last on
 purpose; it passes alone in a fresh process and after the other tests.
 """
 from __future__ import annotations
@@ -94,3 +95,23 @@ def test_no_alloc_attention_refuses_sizes_beyond_its_scratch():
     assert code == 1
     with pytest.raises(MmcError, match="scratch"):
         check(code)
+
+
+def test_no_alloc_attention_reports_device_errors():
+    """The caller cannot reach the error word inside the library's array, so the
+    entry point reports it: a block table with -1 for a needed page returns
+    MMC_ERR_DEVICE (the kernel records the error and skips the page; nothing
+    traps), and the next call with a complete table succeeds again."""
+    c = _case(4, batch=2, ctx=300)
+    bt = c["bt"].clone()
+    bt[0, 1] = -1
+    bad = dict(c, bt=bt)
+    pool = c["pool"].clone()
+    out = torch.empty(c["batch"], c["nq"] * c["hd"], device="cuda")
+    code = lib().mmc_op_attention_noalloc(*_args(bad, pool, out), dev(out), None)
+    assert code == 5
+    assert b"page" in lib().mmc_last_error()
+    ref, _ = _with_workspace(c)
+    got, _ = _no_alloc(c)
+    err = (got - ref).abs()
+    assert (err <= ATOL + RTOL * ref.abs()).all()
