@@ -430,8 +430,8 @@ def main() -> None:
                 "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "peak_source": f"{peak_src} hbm_gbs",
                 # DRAM bytes per launch: the ratio of dram__bytes_read.sum + dram__bytes_write.sum to the
-                # algorithmic bytes in the ncu capture of profiles/attention_hd96_b128_ctx1024.md (a smaller
-                # launch of the same kernel; traffic grows with the pages read), scaled to this launch
+                # algorithmic bytes in an ncu capture of a smaller launch of the same kernel (B=128, ctx 1024,
+                # hd 96; traffic grows with the pages read), scaled to this launch
                 "traffic": attn_bytes_per_launch * ATTN_TRAFFIC_RATIO,
                 "traffic_source": "scaled from an ncu capture of a smaller launch (ratio %.3f)" % ATTN_TRAFFIC_RATIO,
                 "bytes_per_launch": attn_bytes_per_launch, "avg_launch_ms": attn_ms,

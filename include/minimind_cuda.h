@@ -203,6 +203,23 @@ MMC_EXPORT int mmc_graph_set_tokens(mmc_ctx* ctx, const int32_t* tokens_host);
 MMC_EXPORT int mmc_graph_run(mmc_ctx* ctx, int32_t n_steps, void* stream);
 MMC_EXPORT int mmc_graph_tokens(mmc_ctx* ctx, int32_t n_steps, int32_t* tokens_host);
 
+/* Streaming on the device-resident loop (replaces the per-token callback
+ * loop of LanguageModel::generate_stream, language_model.cpp:368-396, whose
+ * tokens the CLI prints as they come, minimind_generate.cpp:95-100):
+ * mmc_graph_stream_start arms `n_steps` replays of the graph built by
+ * mmc_graph_build (tokens set by mmc_graph_set_tokens); each
+ * mmc_graph_stream_next returns the next step's tokens ([batch], host
+ * memory) as soon as that step has finished on the device, while up to 32
+ * later replays are already queued behind it. Each replay is followed by an
+ * async copy of its tokens into a pinned ring, so the loop keeps running on
+ * the device between reads. A position advances when its replay is queued;
+ * mmc_graph_stream_stop (or any other step, prompt pass or graph call) waits
+ * for the queued replays and ends the run early, e.g. at an end-of-sequence
+ * token. */
+MMC_EXPORT int mmc_graph_stream_start(mmc_ctx* ctx, int32_t n_steps);
+MMC_EXPORT int mmc_graph_stream_next(mmc_ctx* ctx, int32_t* tokens_host);
+MMC_EXPORT int mmc_graph_stream_stop(mmc_ctx* ctx);
+
 /* Wait for the context's stream and report any device-side error. */
 MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
 /* Number of kernels one decode step launches for a batch of `batch` rows:

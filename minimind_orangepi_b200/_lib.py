@@ -68,6 +68,9 @@ EXPORTS = {
     "mmc_graph_set_tokens": (C.c_int, [C.c_void_p, C.c_void_p]),
     "mmc_graph_run": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p]),
     "mmc_graph_tokens": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p]),
+    "mmc_graph_stream_start": (C.c_int, [C.c_void_p, C.c_int32]),
+    "mmc_graph_stream_next": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "mmc_graph_stream_stop": (C.c_int, [C.c_void_p]),
     "mmc_synchronize": (C.c_int, [C.c_void_p]),
     "mmc_kernels_per_step": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
     "mmc_op_projection": (C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,

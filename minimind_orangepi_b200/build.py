@@ -124,7 +124,10 @@ def build_oracle() -> None:
     src = oracle / "minimind_oracle.c"
     if _stale(so, [src]):
         _run(["gcc", "-std=c11", "-O3", "-DNDEBUG", "-fPIC", "-shared", "-o", str(so), str(src), "-lm"])
-    ref_root = Path(os.environ.get("MINIMIND_REFERENCE_ROOT", "/root/reference"))
+    # the reference checkout: MINIMIND_REFERENCE_ROOT, else a `reference`
+    # directory beside this repository's own directory
+    env = os.environ.get("MINIMIND_REFERENCE_ROOT")
+    ref_root = Path(env) if env else ROOT.parent / "reference"
     if (ref_root / "src" / "csrc").exists():
         _run(["bash", str(oracle / "build_ref.sh"), str(ref_root)])
 

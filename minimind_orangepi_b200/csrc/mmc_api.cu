@@ -89,6 +89,10 @@ struct Layer {
 
 }  // namespace
 
+// pinned ring slots of the streamed graph loop (steps in flight ahead of the
+// host's reads)
+constexpr int kRingSlots = 32;
+
 struct mmc_ctx {
   mmc_model_desc d{};
   int device = 0;
@@ -155,6 +159,12 @@ struct mmc_ctx {
   int* hist_step = nullptr;
   int hist_cap = 0;
   int64_t graph_cap_tokens = 0;  // positions the captured split plan covers
+
+  // streamed graph loop: each replay is followed by an async copy of its
+  // tokens (and the device error word) into a pinned ring slot and an event
+  int* h_ring = nullptr;  // pinned [kRingSlots][max_batch + 1]
+  cudaEvent_t ring_ev[kRingSlots] = {};
+  int64_t st_total = 0, st_enqueued = 0, st_consumed = 0;
 
   template <typename T>
   T* alloc(size_t n, const char* what) {
@@ -743,8 +753,12 @@ void reserve_pages(mmc_ctx* c, int32_t seq, int64_t tokens) {
          c->h_block_table.data() + size_t(seq) * c->max_pages + old, sizeof(int) * (need - old), "block table upload");
 }
 
+void stream_drain(mmc_ctx* c);
+
 // Host-side checks shared by the eager step entry points; returns the plan.
+// An eager step ends a streamed graph run that is still in progress.
 StepIO plan_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, bool auto_reserve) {
+  stream_drain(c);
   require_ready(c);
   require(batch >= 1 && batch <= c->max_batch, MMC_ERR_INVALID, "batch outside [1, max_batch]");
   require(seq_ids != nullptr, MMC_ERR_INVALID, "null seq_ids");
@@ -976,7 +990,16 @@ void finish_load(mmc_ctx* c) {
   c->loaded = true;
 }
 
+// Ends a streamed run: waits for the replays already enqueued (their steps
+// happened: positions were advanced when they were enqueued).
+void stream_drain(mmc_ctx* c) {
+  if (c->st_enqueued > c->st_consumed) ck(cudaStreamSynchronize(c->stream), "stream drain");
+  c->st_total = c->st_enqueued = c->st_consumed = 0;
+}
+
 void drop_graph(mmc_ctx* c) {
+  if (c->st_total > 0) cudaStreamSynchronize(c->stream);
+  c->st_total = c->st_enqueued = c->st_consumed = 0;
   if (c->graph) cudaGraphExecDestroy(c->graph);
   c->graph = nullptr;
   c->graph_batch = 0;
@@ -1043,6 +1066,9 @@ void mmc_destroy(mmc_ctx* c) {
   drop_graph(c);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->h_ring) cudaFreeHost(c->h_ring);
+  for (auto e : c->ring_ev)
+    if (e) cudaEventDestroy(e);
   for (auto ps : c->part_stream)
     if (ps) cudaStreamSynchronize(ps);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -1424,6 +1450,7 @@ int mmc_prefill(mmc_ctx* c, int32_t n_seqs, const int32_t* seq_ids, const int32_
     use_device(c);
     require_ready(c);
     require(n_seqs >= 1 && seq_ids && prompt_lens && tokens && next_tokens, MMC_ERR_INVALID, "null argument");
+    stream_drain(c);
     // validate everything before anything runs
     int64_t total = 0;
     std::vector<char> seen(c->max_seqs, 0);
@@ -1647,6 +1674,7 @@ int mmc_graph_run(mmc_ctx* c, int32_t n_steps, void* stream) {
     require(c && c->graph, MMC_ERR_STATE, "no graph built");
     use_device(c);
     require(n_steps >= 0 && n_steps <= c->hist_cap, MMC_ERR_INVALID, "n_steps outside [0, 8192]");
+    stream_drain(c);
     for (int s : c->graph_slots) {
       require(c->h_pos[s] + n_steps <= int64_t(c->h_pages[s]) * mmc::kPageTokens, MMC_ERR_NO_PAGES,
               "graph run needs more reserved KV pages (mmc_seq_reserve)");
@@ -1659,6 +1687,79 @@ int mmc_graph_run(mmc_ctx* c, int32_t n_steps, void* stream) {
     ck(cudaMemsetAsync(c->hist_step, 0, kMaxParts * sizeof(int), st), "history reset");
     for (int i = 0; i < n_steps; ++i) ck(cudaGraphLaunch(c->graph, st), "graph launch");
     for (int s : c->graph_slots) c->h_pos[s] += n_steps;
+  });
+}
+
+int mmc_graph_stream_start(mmc_ctx* c, int32_t n_steps) {
+  return guarded([&] {
+    require(c && c->graph, MMC_ERR_STATE, "no graph built");
+    use_device(c);
+    require(n_steps >= 1, MMC_ERR_INVALID, "n_steps must be positive");
+    stream_drain(c);
+    for (int s : c->graph_slots) {
+      require(c->h_pos[s] + n_steps <= int64_t(c->h_pages[s]) * mmc::kPageTokens, MMC_ERR_NO_PAGES,
+              "streamed run needs more reserved KV pages (mmc_seq_reserve)");
+      require(c->h_pos[s] + n_steps <= c->graph_cap_tokens, MMC_ERR_STATE,
+              "streamed run goes past the positions the graph was built for (rebuild it)");
+      require(c->h_pos[s] + n_steps <= c->d.max_position_embeddings, MMC_ERR_OUT_OF_RANGE,
+              "position exceeds max_position_embeddings");
+    }
+    if (!c->h_ring) {
+      ck(cudaHostAlloc(reinterpret_cast<void**>(&c->h_ring), sizeof(int) * kRingSlots * (c->max_batch + 1),
+                       cudaHostAllocDefault),
+         "pinned token ring");
+      for (auto& e : c->ring_ev) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "ring event");
+    }
+    ck(cudaMemsetAsync(c->hist_step, 0, kMaxParts * sizeof(int), c->stream), "history reset");
+    c->st_total = n_steps;
+  });
+}
+
+namespace {
+// keep up to kRingSlots replays (and their token copies) in flight ahead of
+// the host's reads; positions advance as each replay is enqueued
+void stream_top_up(mmc_ctx* c) {
+  const int B = c->graph_batch;
+  while (c->st_enqueued < c->st_total && c->st_enqueued < c->st_consumed + kRingSlots) {
+    const int slot = int(c->st_enqueued % kRingSlots);
+    int* row = c->h_ring + size_t(slot) * (c->max_batch + 1);
+    ck(cudaGraphLaunch(c->graph, c->stream), "graph launch");
+    ck(cudaMemcpyAsync(row, c->tokens, sizeof(int) * B, cudaMemcpyDeviceToHost, c->stream), "D2H step tokens");
+    ck(cudaMemcpyAsync(row + B, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H error word");
+    ck(cudaEventRecord(c->ring_ev[slot], c->stream), "ring event");
+    for (int s : c->graph_slots) c->h_pos[s] += 1;
+    ++c->st_enqueued;
+  }
+}
+}  // namespace
+
+int mmc_graph_stream_next(mmc_ctx* c, int32_t* tokens) {
+  return guarded([&] {
+    require(c && tokens, MMC_ERR_INVALID, "null argument");
+    require(c->graph && c->st_consumed < c->st_total, MMC_ERR_STATE, "no streamed step left (mmc_graph_stream_start)");
+    use_device(c);
+    stream_top_up(c);
+    const int slot = int(c->st_consumed % kRingSlots);
+    ck(cudaEventSynchronize(c->ring_ev[slot]), "streamed step");
+    const int B = c->graph_batch;
+    const int* row = c->h_ring + size_t(slot) * (c->max_batch + 1);
+    if (row[B] != 0) {
+      stream_drain(c);
+      raise_device_error(c, row[B]);
+    }
+    std::memcpy(tokens, row, sizeof(int) * B);
+    ++c->st_consumed;
+    if (c->st_consumed == c->st_total) c->st_total = c->st_enqueued = c->st_consumed = 0;
+    else stream_top_up(c);
+  });
+}
+
+int mmc_graph_stream_stop(mmc_ctx* c) {
+  return guarded([&] {
+    require(c != nullptr, MMC_ERR_INVALID, "null context");
+    use_device(c);
+    stream_drain(c);
+    check_device_error(c);
   });
 }
 

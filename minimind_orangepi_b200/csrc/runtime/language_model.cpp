@@ -44,6 +44,10 @@ mmc_model_desc describe(const MiniMindConfig& c) {
   return d;
 }
 
+// generate_stream runs at least this many decode steps on the streamed graph
+// loop; shorter runs are not worth capturing a graph for
+constexpr int64_t kStreamMinSteps = 8;
+
 int64_t env_i64(const char* name, int64_t fallback) {
   const char* v = std::getenv(name);
   return (v && *v) ? std::strtoll(v, nullptr, 10) : fallback;
@@ -241,11 +245,31 @@ void LanguageModel::generate_stream(const std::vector<int32_t>& prompt_tokens, i
   if (max_new_tokens < 0) throw std::invalid_argument("max_new_tokens cannot be negative");
   DecoderState state = make_state();
   int32_t next = prefill_next_token(prompt_tokens, state);
+  const int64_t steps = max_new_tokens - 1;  // decode steps after the prompt's token
+  if (steps < kStreamMinSteps) {
+    for (int64_t i = 0; i < max_new_tokens; ++i) {
+      on_token(next);
+      if (next == config_.eos_token_id || i + 1 == max_new_tokens) break;
+      next = forward_next_token(next, state);
+    }
+    return;
+  }
+  // Longer runs stay on the captured device loop: the graph feeds each
+  // step's token to the next on the device, and every step's token reaches
+  // the host through a pinned ring as soon as that step finishes, so the
+  // callback sees tokens while later steps are already running.
+  mmc_ctx* ctx = device_->ctx();
+  const int32_t seq = state.device->id();
+  mmc_check(mmc_seq_reserve(ctx, seq, state.position + steps + 1));
+  mmc_check(mmc_graph_build(ctx, 1, &seq));
+  mmc_check(mmc_graph_set_tokens(ctx, &next));
+  mmc_check(mmc_graph_stream_start(ctx, static_cast<int32_t>(steps)));
   for (int64_t i = 0; i < max_new_tokens; ++i) {
     on_token(next);
     if (next == config_.eos_token_id || i + 1 == max_new_tokens) break;
-    next = forward_next_token(next, state);
+    mmc_check(mmc_graph_stream_next(ctx, &next));
   }
+  mmc_check(mmc_graph_stream_stop(ctx));
 }
 
 std::vector<int32_t> LanguageModel::generate(const std::vector<int32_t>& prompt_tokens, int64_t max_new_tokens) const {

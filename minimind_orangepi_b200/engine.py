@@ -253,6 +253,51 @@ class DecodeEngine:
                                  first.ctypes.data))
         return first
 
+    def graph_stream(self, n_steps: int):
+        """Streams n_steps replays of the built graph: yields each step's
+        tokens ([batch]) as soon as that step has finished on the device, while
+        later steps are already queued (mmc_graph_stream_*). Closing the
+        generator early stops the run after the steps already queued."""
+        check(self.L.mmc_graph_stream_start(self.h, n_steps))
+        out = np.empty(len(self._graph_seqs), np.int32)
+        try:
+            for _ in range(n_steps):
+                check(self.L.mmc_graph_stream_next(self.h, out.ctypes.data))
+                yield out.copy()
+        finally:
+            check(self.L.mmc_graph_stream_stop(self.h))
+
+    def generate_stream(self, prompt, max_new_tokens: int, eos: int | None = None):
+        """LanguageModel::generate_stream on the device: yields each generated
+        token as it is produced (greedy, stops after eos), the prompt in one
+        device pass and the decode steps on the streamed graph loop."""
+        if not prompt:
+            raise ValueError("prompt_tokens cannot be empty")
+        if max_new_tokens < 0:
+            raise ValueError("max_new_tokens cannot be negative")
+        if max_new_tokens == 0:
+            return
+        eos = self.config.eos_token_id if eos is None else eos
+        seq = self.open_sequence(len(prompt) + max_new_tokens + 1)
+        try:
+            nxt = int(self.prompt_pass([seq], [list(prompt)])[0])
+            yield nxt
+            if nxt == eos or max_new_tokens == 1:
+                return
+            self.graph_build([seq])
+            self.graph_set_tokens([nxt])
+            stream = self.graph_stream(max_new_tokens - 1)
+            try:
+                for toks in stream:
+                    nxt = int(toks[0])
+                    yield nxt
+                    if nxt == eos:
+                        return
+            finally:
+                stream.close()
+        finally:
+            self.close_sequence(seq)
+
     def generate(self, prompt, max_new_tokens: int, eos: int | None = None):
         """LanguageModel::generate on the device (greedy, eos stop)."""
         if not prompt:

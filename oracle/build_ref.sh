@@ -12,10 +12,11 @@
 #      symbols (cube_*_available() == false, so the CPU path is taken).
 # Flags follow the reference's Release build (-O3 -DNDEBUG, C++17), no -march,
 # no fast-math, so float arithmetic is plain IEEE SSE2.
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+#   (default: $MINIMIND_REFERENCE_ROOT, else `reference` beside this repository)
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF="${1:-${MINIMIND_REFERENCE_ROOT:-/root/reference}}"
+REF="${1:-${MINIMIND_REFERENCE_ROOT:-$(cd "$HERE/../.." && pwd)/reference}}"
 SRC="$REF/src/csrc"
 OUT="$HERE/_ref"
 if [ ! -d "$SRC/models/minimind" ]; then

@@ -1,5 +1,6 @@
 """The drop-in surface on the GPU: the minimind_generate / bench_decode CLIs
-(C++ LanguageModel over the C ABI) and the Python TextSession, on a seeded
+(C++ LanguageModel over the C ABI), DecodeEngine streaming and the in-process
+TextSession, on a seeded
 MiniMind2-small model, against the reference's own greedy output (golden
 fixture made by the reference CPU path)."""
 from __future__ import annotations
@@ -52,13 +53,31 @@ def test_cli_generate_matches_reference(model):
     _same_until_near_tie(got, *_expected())
 
 
-def test_cli_stream_lines(model):
-    out = subprocess.run([str(BIN / "minimind_generate"), "--model", str(model), "--tokens", "5,6,7",
-                          "--max-new-tokens", "6", "--stream"], capture_output=True, text=True, check=True).stdout
-    toks = [l for l in out.splitlines() if l.startswith("token:")]
+@pytest.mark.parametrize("new_tokens", [6, 40])
+def test_cli_stream_equals_blocking(model, new_tokens):
+    """--stream prints one token: line per token; 40 tokens run on the streamed
+    graph loop (6 on eager steps). Both must equal the blocking output."""
+    cmd = [str(BIN / "minimind_generate"), "--model", str(model), "--tokens", "5,6,7", "--max-new-tokens",
+           str(new_tokens)]
+    out = subprocess.run(cmd + ["--stream"], capture_output=True, text=True, check=True).stdout
+    blocking = subprocess.run(cmd, capture_output=True, text=True, check=True).stdout
+    toks = [int(l.split()[1]) for l in out.splitlines() if l.startswith("token:")]
     final = [l for l in out.splitlines() if l.startswith("generated_tokens:")][0]
-    assert len(toks) == len(final.split(":", 1)[1].split()) <= 6
-    assert [int(l.split()[1]) for l in toks] == [int(t) for t in final.split(":", 1)[1].split()]
+    assert toks == [int(t) for t in final.split(":", 1)[1].split()]
+    assert len(toks) <= new_tokens
+    assert final == blocking.splitlines()[-1]
+
+
+def test_engine_stream_matches_reference(model):
+    """DecodeEngine.generate_stream (prompt pass + streamed graph loop) yields
+    the reference's greedy tokens, one at a time."""
+    from minimind_orangepi_b200 import DecodeEngine
+
+    with DecodeEngine(model, max_seqs=2, max_batch=1) as eng:
+        got = list(eng.generate_stream([int(t) for t in G["prompt"]], len(G["generated"]), eos=-1))
+        again = eng.generate([int(t) for t in G["prompt"]], len(G["generated"]), eos=-1)
+    assert got == again
+    _same_until_near_tie(got, *_expected())
 
 
 @pytest.mark.parametrize("batch", [1, 8])
@@ -73,9 +92,11 @@ def test_bench_decode_reports_the_reference_keys(model, batch):
     assert kv["decode_steps"] == "15" and float(kv["decode_tokens_per_second"]) > 0
 
 
-def test_text_session_over_the_cuda_cli(model):
-    s = TextSession(None, model)
-    blocking = s.generate_result("hello", 5)
-    streamed = list(s.stream_generate_result("hello", 5))
+def test_text_session_in_process(model):
+    """The in-process session: streamed results end with the blocking result."""
+    with TextSession(model) as s:
+        blocking = s.generate_result("hello", 12)
+        streamed = list(s.stream_generate_result("hello", 12))
     assert streamed[-1].generated_tokens == blocking.generated_tokens
+    assert streamed[-1].raw_output.endswith(blocking.raw_output.splitlines()[-1] + "\n")
     assert blocking.prompt_tokens == [ord(c) for c in "hello"]

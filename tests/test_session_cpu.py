@@ -68,35 +68,66 @@ def test_validate_runtime_model_dir(tmp_path):
     validate_runtime_model_dir(d)
 
 
+class FakeEngine:
+    """Stands in for DecodeEngine: a deterministic greedy stream (no GPU)."""
+
+    class config:
+        vocab_size = 8
+        bos_token_id = 1
+        eos_token_id = 2
+
+    def __init__(self):
+        self.calls = []
+
+    def generate_stream(self, prompt, max_new_tokens, eos=None):
+        self.calls.append((list(prompt), max_new_tokens))
+        for i in range(max_new_tokens):
+            t = (prompt[-1] + 3 * i + 3) % 8
+            yield t
+            if t == self.config.eos_token_id:
+                return
+
+
 @pytest.fixture
-def fake_cli(tmp_path):
-    """A stand-in for minimind_generate with the same flags and output lines."""
-    script = tmp_path / "fake_generate"
-    script.write_text(f"""#!{sys.executable}
-import sys
-a = sys.argv[1:]
-n = int(a[a.index('--max-new-tokens') + 1])
-toks = [int(t) for t in a[a.index('--tokens') + 1].split(',')] if '--tokens' in a else [ord(c) for c in a[a.index('--prompt') + 1]]
-print('prompt_tokens: ' + ' '.join(map(str, toks)), flush=True)
-gen = [(toks[-1] + i + 1) % 8 for i in range(n)]
-if '--stream' in a:
-    for t in gen:
-        print(f'token: {{t}}', flush=True)
-print('generated_tokens: ' + ' '.join(map(str, gen)), flush=True)
-""")
-    script.chmod(0o755)
-    return script
+def model_dir_stub(tmp_path):
+    d = tmp_path / "model"
+    d.mkdir()
+    (d / "minimind_runtime_config.txt").write_text("hidden_size=64\n")
+    (d / "weights.bin").write_bytes(b"MMRTW001")
+    return d
 
 
-def test_text_session_stream_matches_blocking(fake_cli):
-    s = TextSession(fake_cli, None)
+def test_text_session_stream_matches_blocking(model_dir_stub):
+    eng = FakeEngine()
+    s = TextSession(model_dir_stub, engine=eng)
     streamed = list(s.stream_generate_result("hi", 3))
     blocking = s.generate_result("hi", 3)
-    assert len(streamed) == 4  # three token lines + the final summary line
+    # byte fallback folded into the vocabulary, as the CLI does
+    assert blocking.prompt_tokens == [ord("h") % 8, ord("i") % 8]
+    assert len(streamed) == len(blocking.generated_tokens) + 1  # token lines + the final summary
     assert streamed[-1].generated_tokens == blocking.generated_tokens
-    assert streamed[-1].prompt_tokens == blocking.prompt_tokens == [ord("h"), ord("i")]
+    assert streamed[-1].prompt_tokens == blocking.prompt_tokens
+    # raw output in the CLI's line format, parseable by the same helpers
+    assert parse_token_line(blocking.raw_output, "generated_tokens") == blocking.generated_tokens
+    assert [parse_stream_token_line(ln) for ln in streamed[-1].raw_output.splitlines() if ln.startswith("token:")] \
+        == blocking.generated_tokens
+    assert streamed[-1].format() == streamed[-1].raw_output  # no tokenizer -> no text line
     chat = list(s.stream_generate_chat_result([("hi", "hello"), ("who", "")], 2))
     assert chat[-1].generated_tokens and "generated_tokens" in chat[-1].raw_output
+    # the chat prompt is passed raw (markers already applied)
+    assert eng.calls[-1][0] == [b % 8 for b in chat_prompt_from_history([("hi", "hello"), ("who", "")]).encode()]
+
+
+def test_text_session_stops_at_eos_and_empty_prompt(model_dir_stub):
+    s = TextSession(model_dir_stub, engine=FakeEngine())
+    r = s.generate_result("\x05", 10)  # 5 -> 0, 3, 6, 1, 4, 7, 2 (eos)
+    assert r.generated_tokens[-1] == 2 and len(r.generated_tokens) < 10
+    assert s.generate_result("", 1).prompt_tokens == [1]  # empty prompt -> bos
+
+
+def test_text_session_requires_a_runtime_model(tmp_path):
+    with pytest.raises(FileNotFoundError):
+        TextSession(tmp_path / "missing")
 
 
 @pytest.mark.skipif(not CLI.exists(), reason="CLI not built")
