@@ -322,6 +322,12 @@ def main() -> None:
     eng.graph_run(W, sptr)
     torch.cuda.synchronize()
 
+    # algorithmic bytes of the timed steps (weights once per step, every cached
+    # K/V row read, one row appended per sequence and layer)
+    pos0 = [eng.position(sq) for sq in seqs]
+    kvb = kv_bytes_per_position(shape)
+    timed_bytes = K * weight_bytes(shape) + sum(sum(p + i + 1 for i in range(K)) * kvb + K * kvb for p in pos0)
+
     # ---------------- timed: K graph replays, device events, max over ranks
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
@@ -368,6 +374,7 @@ def main() -> None:
     kernels_per_step = eng.kernels_per_step(B)
 
     # ---------------- reduce over ranks
+    persistent = kernels_per_step == 1  # the whole step is one launch (batches of up to 64 rows)
     vals = np.array([dev_ms, e2e_s * 1000.0, attn_ms], np.float64)
     if dist:
         t = torch.tensor(vals, device="cuda")
@@ -426,6 +433,13 @@ def main() -> None:
                             "graph replay, D2H next tokens, synchronous)"},
             "gpu_launches": kernels_per_step * K,
             "roofline": {
+                "bound": "hbm", "kernel": "persistent decode step (the whole step in one launch)",
+                "achieved": timed_bytes / (dev_ms / 1000.0) / 1e9, "peak": hbm, "unit": "GB/s",
+                "frac": timed_bytes / (dev_ms / 1000.0) / 1e9 / hbm, "peak_source": f"{peak_src} hbm_gbs",
+                "traffic": None, "bytes_per_launch": timed_bytes / K, "avg_launch_ms": dev_ms / K,
+                "note": "one launch per step: achieved = algorithmic bytes of the timed steps (weights, every cached "
+                        "K/V row, appended rows) / their device time",
+            } if persistent else {
                 "bound": "hbm", "kernel": "attention (fused q/k norm + RoPE + paged KV append + flash-decode)",
                 "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "peak_source": f"{peak_src} hbm_gbs",

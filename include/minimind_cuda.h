@@ -129,6 +129,13 @@ MMC_EXPORT int mmc_debug_fill_kv(mmc_ctx* ctx, int32_t seq, int64_t n_tokens, ui
  * 3 SiLU*mul activations [batch][intermediate]. `count` floats are copied. */
 MMC_EXPORT int mmc_debug_scratch(mmc_ctx* ctx, int32_t which, float* host, int64_t count);
 
+/* Debug helper for the persistent step (batches of up to 64 rows): with
+ * MMC_STEP_TRACE=1 set when the context was created, each step records per
+ * task global-timer nanoseconds (CTA, start, dependencies met, computed,
+ * signalled, three unused); this copies the last step's records ([n][8]
+ * uint64) to host memory and reports the step's task count. */
+MMC_EXPORT int mmc_debug_step_trace(mmc_ctx* ctx, uint64_t* host, int64_t max_tasks, int64_t* n_tasks);
+
 /* ------------------------------------------------------------- decode */
 
 /* One greedy decode step for `batch` sequences — the batched form of
@@ -223,8 +230,10 @@ MMC_EXPORT int mmc_graph_stream_stop(mmc_ctx* ctx);
 /* Wait for the context's stream and report any device-side error. */
 MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
 /* Number of kernels one decode step launches for a batch of `batch` rows:
- * 6 per layer + 1 for batch <= 4; above, 6 per layer + 2 for each of the
- * concurrent parts the batch runs as (up to 4 parts of >= 64 rows). */
+ * 1 for batches of up to 64 rows on dense models (the persistent step:
+ * the whole step is one cooperative launch); otherwise 6 per layer + 1 for
+ * batch <= 4, and above, 6 per layer + 2 for each of the concurrent parts the
+ * batch runs as (up to 4 parts of >= 64 rows). */
 MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* kernels);
 
 /* ------------------------------------------------------------- single ops

@@ -55,6 +55,7 @@ EXPORTS = {
     "mmc_debug_read_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     "mmc_debug_fill_kv": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_uint32]),
     "mmc_debug_scratch": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int64]),
+    "mmc_debug_step_trace": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(C.c_int64)]),
     "mmc_decode_step": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "mmc_configure_moe": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64]),
     "mmc_save_packed": (C.c_int, [C.c_void_p, C.c_char_p]),

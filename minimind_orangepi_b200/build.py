@@ -38,6 +38,7 @@ CUDA_SOURCES = [
     CSRC / "kernels" / "mlp_chain.cu",
     CSRC / "kernels" / "attention.cu",
     CSRC / "kernels" / "pack.cu",
+    CSRC / "kernels" / "step_kernel.cu",
     CSRC / "mmc_api.cu",
     CSRC / "attention_noalloc.cu",
 ]

@@ -112,7 +112,7 @@ __device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, StageMeta&
   const int per_split = a.B * a.nkv;
   m.split = w / per_split;
   const int bh = w % per_split;
-  m.b = bh / a.nkv;
+  m.b = a.order ? a.order[bh / a.nkv] : bh / a.nkv;
   m.h = bh % a.nkv;
   const int ctx = a.seq_pos[a.slots[m.b]] + (a.row_off ? a.row_off[m.b] : 0) + 1;
   const int pages = (ctx + kPageTokens - 1) / kPageTokens;

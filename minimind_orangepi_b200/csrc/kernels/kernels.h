@@ -183,6 +183,7 @@ struct AttnArgs {
   const int* seq_pos = nullptr;  // [max_seqs] tokens cached before this step
   const int* slots = nullptr;    // [B]
   const int* row_off = nullptr;  // optional [B]: row b sits at seq_pos[slots[b]] + row_off[b] (prompt pass)
+  const int* order = nullptr;    // optional [B]: work-queue order of the rows (longest work items first)
   int B = 0, nq = 0, nkv = 0, hd = 0;
   int split_tokens = 0;  // multiple of the page size
   int max_splits = 0;    // grid.x
@@ -199,6 +200,79 @@ constexpr int kPageTokens = 64;
 size_t attn_part_floats(int B, int nkv, int max_splits, int rep, int hd);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t attention_init_attributes();
+
+// Persistent decode step for small batches (step_kernel.cu): the whole step --
+// embedding gather, every layer's q|k|v projection, q/k norm + RoPE + KV
+// append + split-KV attention, o projection, gate/up + SwiGLU, down
+// projection, and lm_head + argmax -- as ONE cooperative launch of one CTA per
+// SM. The rows run as independent groups of up to 32; the step is a list of
+// tasks (stage, group, tile) dealt round-robin to the CTAs, each task waiting
+// on a per-(group, stage) completion counter instead of a kernel boundary,
+// while a producer warp per CTA prefetches the weight tiles and KV pages of
+// the CTA's next tasks into a shared-memory ring.
+constexpr int kStepGroupRows = 32;
+constexpr int kStepMaxGroups = 2;
+constexpr int kStepRingBytes = 136 * 1024;  // per-CTA prefetch ring
+constexpr int kStepMaxLayers = 32;
+constexpr int kStepMaxStages = 2 + 5 * kStepMaxLayers;
+constexpr int kStepSyncWords = 1024;
+constexpr int kStepMaxK = 2048;  // longest input row the step supports
+struct StepLayer {
+  const __half* qkv = nullptr;   // fragment order (launch_pack_fragments) of the fused [q; k; v] rows
+  const __half* o = nullptr;
+  const __half* gu = nullptr;    // gate/up interleaved by 8 rows
+  const __half* down = nullptr;
+  const float* q_norm = nullptr;
+  const float* k_norm = nullptr;
+};
+struct StepArgs {
+  StepLayer layer[kStepMaxLayers];
+  const __half* lm = nullptr;  // fragment order, final norm folded in
+  const float* embed = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  __half* kv_pool = nullptr;
+  const int* block_table = nullptr;
+  int max_pages = 0;
+  int* seq_pos = nullptr;
+  const int* slots = nullptr;
+  int* tokens = nullptr;    // [B] in: this step's tokens, out: next tokens
+  int* next_out = nullptr;  // optional [B]
+  float* logits = nullptr;  // optional [B][V]
+  int* hist = nullptr;
+  int* hist_step = nullptr;
+  int hist_cap = 0, hist_stride = 0;
+  int B = 0, H = 0, NQKV = 0, I = 0, V = 0, L = 0, nq = 0, nkv = 0, hd = 0, max_pos = 0;
+  float eps = 0.f;
+  // scratch
+  float* h = nullptr;       // [B][H] residual stream
+  __half* h16 = nullptr;    // [B][H]
+  float* ssp = nullptr;     // [B][H / 16] sums of squares of 16-column chunks of h
+  float* qkv = nullptr;     // [B][NQKV] raw projections (scaled by 1/rms)
+  __half* attn16 = nullptr; // [B][nq * hd]
+  __half* act16 = nullptr;  // [B][I]
+  float* part = nullptr;    // [B][nkv][s_max][rep][hd + 2] attention job partials
+  unsigned* arrive = nullptr;  // [B][nkv] job arrival counters (self-resetting)
+  void* lm_part = nullptr;     // [groups][lm tasks][kStepGroupRows] (value, index)
+  unsigned* sync = nullptr;    // kStepSyncWords zeroed words (self-resetting)
+  // attention: pages per chunk (one ring entry), jobs per (row, kv head), chunks per job
+  int split_pages = 1, s_max = 1, job_chunks = 1;
+  int groups = 0, stages = 0, total_tasks = 0;
+  int tiles[8] = {0};  // 16-row weight tiles per task, by task type (set by step_plan)
+  int tasks[8] = {0};  // tile groups per stage, by task type (set by step_plan)
+  int offs[kStepMaxStages * kStepMaxGroups + 1];  // first task of (stage, group), set by step_plan
+  unsigned long long* trace = nullptr;  // optional [total_tasks][8] timestamps (ns), see mmc_debug_step_trace
+  int* err = nullptr;
+};
+// attention pages per chunk the ring can hold for head_dim hd
+int step_max_split_pages(int hd);
+// fills the attention plan (from the longest context the step may see), groups and the task table
+void step_plan(StepArgs& a, int64_t max_ctx_tokens, int num_sms);
+cudaError_t launch_step(const StepArgs& a, int num_sms, cudaStream_t stream);
+cudaError_t step_init_attributes();
+// fragment order of a row-major fp16 [N][K] matrix (N % 16 == 0, K % 16 == 0):
+// per 16-row tile, per 16-column step, the 32 lanes' m16n8k16 A fragments (16 B each)
+cudaError_t launch_pack_fragments(const __half* src, __half* dst, int64_t N, int64_t K, cudaStream_t s);
 
 // Weight packing: fp32 source rows -> fp16 destination rows (RNE), with an
 // optional gate/up interleave by blocks of 8 rows.

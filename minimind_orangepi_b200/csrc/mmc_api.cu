@@ -74,6 +74,8 @@ T* dalloc(size_t count, const char* what) {
 }
 
 constexpr int kMaxParts = 8;
+// batches of up to this many rows run as one persistent launch per step
+constexpr int kStepMaxRows = mmc::kStepGroupRows * mmc::kStepMaxGroups;
 
 int env_int(const char* name, int dflt) {
   const char* v = std::getenv(name);
@@ -85,6 +87,8 @@ struct Layer {
   __half *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
   __half* router = nullptr;                 // MoE: [experts][H] (post-attention norm folded in)
   std::vector<__half*> egu, edown;          // MoE: per expert [2 MI][H] (interleaved, folded), [H][MI]
+  // the same dense projections in fragment order for the persistent step
+  __half *qkv_f = nullptr, *o_f = nullptr, *gu_f = nullptr, *down_f = nullptr;
 };
 
 }  // namespace
@@ -135,6 +139,8 @@ struct mmc_ctx {
   __half* q16 = nullptr;  // normalised + rotated q heads, [max_batch][nq][hd]
   int *tokens = nullptr, *slots = nullptr, *next = nullptr;
   int* row_off = nullptr;  // [max_batch] prompt-pass position offsets
+  int* attn_order = nullptr;  // [max_batch] per batch part: its rows, longest attention work items first
+  int* h_order = nullptr;     // pinned staging of attn_order
   void* argmax_part = nullptr;
   unsigned* argmax_counter = nullptr;
   float* attn_part = nullptr;
@@ -146,6 +152,18 @@ struct mmc_ctx {
   int chain_words = 0;
   bool mlp_chain = false;  // MMC_MLP_CHAIN at creation
   float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
+  // persistent step (batches of up to kStepMaxRows rows, dense models)
+  bool persistent = true;  // MMC_PERSISTENT at creation (default on)
+  __half* lm_f = nullptr;
+  float* step_ssp = nullptr;       // [rows][H / 16]
+  float* step_part = nullptr;      // [rows][nkv][max_pages][rep][hd + 2]
+  unsigned* step_arrive = nullptr; // [rows][nkv]
+  void* step_lm_part = nullptr;    // [groups][V / 16][32] (value, index)
+  unsigned* step_sync = nullptr;   // kStepSyncWords
+  bool step_trace_on = false;      // MMC_STEP_TRACE at creation
+  unsigned long long* step_trace = nullptr;
+  int64_t step_trace_cap = 0;
+  int step_trace_tasks = 0;
   int* err = nullptr;
   int* h_stage = nullptr;  // pinned: [2][max_batch] ints
   int max_splits_cap = 64;
@@ -257,6 +275,7 @@ struct StepIO {
   int64_t total_pages = 1, max_ctx = 1;  // attention plan inputs (whole batch)
   int attn_ctas_per_sm = 2;  // persistent attention CTAs per SM (1 when concurrent batch parts share the GPU)
   const int* row_off = nullptr;  // prompt pass: per-row position offsets (positions advanced by the host)
+  const int* order = nullptr;    // [B] device: per batch part, the part's rows in attention work-queue order
   bool alone = true;  // the batch runs as one part (nothing concurrent competes for the SMs)
   int row0 = 0;  // first scratch row of this part of the batch
   int part = 0;  // 0 .. kMaxParts-1: which counter region this part uses
@@ -428,6 +447,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     a.max_pages = c->max_pages;
     a.seq_pos = c->d_seq_pos;
     a.row_off = io.row_off;
+    a.order = io.order ? io.order + io.row0 : nullptr;
     a.slots = io.slots;
     a.B = io.B;
     a.nq = int(d.num_attention_heads);
@@ -670,7 +690,103 @@ void part_rows(int B, int p, int i, int* r0, int* n) {
   *n = cut(i + 1) - *r0;
 }
 
+// Attention work-queue order (a scheduling hint; any permutation gives the
+// same results): per batch part, its rows sorted by the size of their work
+// items (pages per split under the part's split plan), longest first, so the
+// persistent attention kernel hands out the long items before the short ones
+// and its tail is short. Fills host[0, B) with part-relative row indices.
+void fill_attn_order(const mmc_ctx* c, const StepIO& io, const int32_t* seq_ids, int* host) {
+  const int P = batch_parts(c, io.B);
+  for (int i = 0; i < P; ++i) {
+    int r0 = 0, n = io.B;
+    if (P > 1) part_rows(io.B, P, i, &r0, &n);
+    int max_splits = 1;
+    const int64_t part_pages = P > 1 ? std::max<int64_t>(1, io.total_pages * n / io.B) : io.total_pages;
+    const int split_pages = plan_split(c, part_pages, io.max_ctx, &max_splits) / mmc::kPageTokens;
+    std::vector<std::pair<int64_t, int>> key(static_cast<size_t>(n));
+    for (int b = 0; b < n; ++b) {
+      const int64_t pages = (c->h_pos[seq_ids[r0 + b]] + 1 + mmc::kPageTokens - 1) / mmc::kPageTokens;
+      const int64_t splits = (pages + split_pages - 1) / split_pages;
+      key[size_t(b)] = {-((pages + splits - 1) / splits), b};
+    }
+    std::stable_sort(key.begin(), key.end());
+    for (int b = 0; b < n; ++b) host[r0 + b] = key[size_t(b)].second;
+  }
+}
+
+bool use_step(const mmc_ctx* c, const StepIO& io) {
+  return c->lm_f != nullptr && c->step_sync != nullptr && io.B <= kStepMaxRows && io.row_off == nullptr;
+}
+
+// The whole decode step as one persistent launch (step_kernel.cu).
+void enqueue_persistent(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
+  const auto& d = c->d;
+  mmc::StepArgs a;
+  for (int l = 0; l < int(d.num_hidden_layers); ++l) {
+    const Layer& L = c->layers[l];
+    a.layer[l].qkv = L.qkv_f;
+    a.layer[l].o = L.o_f;
+    a.layer[l].gu = L.gu_f;
+    a.layer[l].down = L.down_f;
+    a.layer[l].q_norm = L.q_norm;
+    a.layer[l].k_norm = L.k_norm;
+  }
+  a.lm = c->lm_f;
+  a.embed = c->embed;
+  a.rope_cos = c->rope_cos;
+  a.rope_sin = c->rope_sin;
+  a.kv_pool = c->kv_pool;
+  a.block_table = c->d_block_table;
+  a.max_pages = c->max_pages;
+  a.seq_pos = c->d_seq_pos;
+  a.slots = io.slots;
+  a.tokens = io.tokens;
+  a.next_out = io.next_out;
+  a.logits = io.logits;
+  a.hist = io.hist;
+  a.hist_step = io.hist_step;
+  a.hist_cap = io.hist_cap;
+  a.hist_stride = io.hist_stride > 0 ? io.hist_stride : io.B;
+  a.B = io.B;
+  a.H = int(d.hidden_size);
+  a.NQKV = c->q_size() + 2 * c->kv_size();
+  a.I = int(d.intermediate_size);
+  a.V = int(d.vocab_size);
+  a.L = int(d.num_hidden_layers);
+  a.nq = int(d.num_attention_heads);
+  a.nkv = int(d.num_key_value_heads);
+  a.hd = int(d.head_dim);
+  a.max_pos = int(d.max_position_embeddings);
+  a.eps = d.rms_norm_eps;
+  a.h = c->hidden;
+  a.h16 = c->h16;
+  a.ssp = c->step_ssp;
+  a.qkv = c->qkv;
+  a.attn16 = c->attn16;
+  a.act16 = c->act16;
+  a.part = c->step_part;
+  a.arrive = c->step_arrive;
+  a.lm_part = c->step_lm_part;
+  a.sync = c->step_sync;
+  a.err = c->err;
+  mmc::step_plan(a, io.max_ctx, c->num_sms);
+  require(a.s_max <= c->max_pages, MMC_ERR_INVALID, "persistent step split plan exceeds its partial buffer");
+  if (c->step_trace_on) {  // debug: per-task timestamps of the last step (mmc_debug_step_trace)
+    if (c->step_trace_cap < int64_t(a.total_tasks)) {
+      c->step_trace_cap = int64_t(a.total_tasks);
+      c->step_trace = c->alloc<unsigned long long>(size_t(c->step_trace_cap) * 8, "step trace");
+    }
+    a.trace = c->step_trace;
+    c->step_trace_tasks = a.total_tasks;
+  }
+  ck(mmc::launch_step(a, c->num_sms, s), "persistent step launch");
+}
+
 void enqueue_batch(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
+  if (use_step(c, io)) {
+    enqueue_persistent(c, io, s);
+    return;
+  }
   const int64_t total_pages = io.total_pages, max_ctx = io.max_ctx;
   const int P = batch_parts(c, io.B);
   if (P == 1) {
@@ -842,6 +958,15 @@ std::string tensor_name(const mmc_ctx* c, int i) {
 
 void finish_load(mmc_ctx* c);
 
+// Whether the model's shapes fit the persistent step kernel (step_kernel.cu).
+bool step_shape_ok(const mmc_ctx* c) {
+  const auto& d = c->d;
+  const int64_t Q = c->q_size(), NQKV = Q + 2 * c->kv_size();
+  return d.num_hidden_layers <= mmc::kStepMaxLayers && (d.head_dim == 64 || d.head_dim == 96 || d.head_dim == 128) &&
+         c->rep() <= 6 && d.hidden_size % 16 == 0 && NQKV % 16 == 0 && d.vocab_size % 16 == 0 &&
+         d.hidden_size <= mmc::kStepMaxK && d.intermediate_size <= mmc::kStepMaxK && Q <= mmc::kStepMaxK;
+}
+
 // Every packed weight buffer of a loaded context, in the order of the packed
 // cache file: (device pointer slot, bytes). With allocate, the buffers are
 // allocated first (loading a cache).
@@ -980,6 +1105,21 @@ void upload_weights(mmc_ctx* c, Getter&& get) {
 // RoPE tables and the loaded flag (after the weight buffers are filled).
 void finish_load(mmc_ctx* c) {
   const auto& d = c->d;
+  if (c->persistent && c->moe_experts == 0 && step_shape_ok(c)) {
+    const int64_t H = d.hidden_size, I = d.intermediate_size, Q = c->q_size(), NQKV = Q + 2 * c->kv_size();
+    auto frag = [&](const __half* src, int64_t N, int64_t K) {
+      __half* dst = c->alloc<__half>(size_t(N * K), "fragment-order weights");
+      ck(mmc::launch_pack_fragments(src, dst, N, K, c->stream), "fragment packing");
+      return dst;
+    };
+    for (auto& L : c->layers) {
+      L.qkv_f = frag(L.qkv, NQKV, H);
+      L.o_f = frag(L.o, H, Q);
+      L.gu_f = frag(L.gu, 2 * I, H);
+      L.down_f = frag(L.down, H, I);
+    }
+    c->lm_f = frag(c->lm_head, d.vocab_size, H);
+  }
   const auto cos_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, false);
   const auto sin_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, true);
   c->rope_cos = c->alloc<float>(cos_t.size(), "rope");
@@ -1049,6 +1189,9 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     ck(cudaEventCreateWithFlags(&c->fork_ev, cudaEventDisableTiming), "event");
     c->split_parts = std::max(1, std::min(kMaxParts, env_int("MMC_SPLIT_BATCH", 4)));
     c->mlp_chain = env_int("MMC_MLP_CHAIN", 0) != 0;
+    c->persistent = env_int("MMC_PERSISTENT", 1) != 0;
+    c->step_trace_on = env_int("MMC_STEP_TRACE", 0) != 0;
+    ck(mmc::step_init_attributes(), "persistent step attributes");
     ck(mmc::gemv_init_attributes(), "gemv attributes");
     ck(mmc::gemm_tc_init_attributes(), "tensor-core projection attributes");
     ck(mmc::mlp_chain_init_attributes(), "projection chain attributes");
@@ -1066,6 +1209,7 @@ void mmc_destroy(mmc_ctx* c) {
   drop_graph(c);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->h_order) cudaFreeHost(c->h_order);
   if (c->h_ring) cudaFreeHost(c->h_ring);
   for (auto e : c->ring_ev)
     if (e) cudaEventDestroy(e);
@@ -1249,6 +1393,8 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->slots = c->alloc<int>(size_t(max_batch), "slots");
     c->next = c->alloc<int>(size_t(max_batch), "next");
     c->row_off = c->alloc<int>(size_t(max_batch), "prompt row offsets");
+    c->attn_order = c->alloc<int>(size_t(max_batch), "attention row order");
+    ck(cudaMallocHost(&c->h_order, sizeof(int) * size_t(max_batch)), "pinned attention row order");
     size_t part_bytes = 0;
     for (int b = 1; b <= std::min(max_batch, 4); ++b)
       part_bytes = std::max(part_bytes, mmc::gemv_argmax_part_bytes(V, H, b, c->num_sms));
@@ -1263,6 +1409,17 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->chain_words = mmc::chain_sync_words(max_batch);
     c->chain_sync = c->alloc<unsigned>(size_t(kMaxParts) * c->chain_words, "projection-chain queues (per batch part)");
     c->ss = c->alloc<float>(size_t(max_batch) * ((H + 127) / 128), "residual sums of squares");
+    if (c->lm_f != nullptr) {  // persistent step scratch (its batches have at most kStepMaxRows rows)
+      const size_t rows = size_t(std::min(max_batch, kStepMaxRows));
+      c->step_ssp = c->alloc<float>(rows * (H / 16), "step sums of squares");
+      c->step_part = c->alloc<float>(rows * d.num_key_value_heads * size_t(c->max_pages) * c->rep() *
+                                         size_t(d.head_dim + 2),
+                                     "step attention partials");
+      c->step_arrive = c->alloc<unsigned>(rows * d.num_key_value_heads, "step job arrivals");
+      c->step_lm_part = c->alloc<uint8_t>(size_t(mmc::kStepMaxGroups) * (V / 16) * mmc::kStepGroupRows * 8,
+                                          "step argmax partials");
+      c->step_sync = c->alloc<unsigned>(mmc::kStepSyncWords, "step counters");
+    }
     ck(cudaMallocHost(&c->h_stage, sizeof(int) * 4 * size_t(max_batch)), "pinned staging");
     ck(cudaDeviceSynchronize(), "KV init");
     c->kv_ready = true;
@@ -1399,6 +1556,18 @@ int mmc_debug_scratch(mmc_ctx* c, int32_t which, float* host, int64_t count) {
   });
 }
 
+int mmc_debug_step_trace(mmc_ctx* c, uint64_t* host, int64_t max_tasks, int64_t* n_tasks) {
+  return guarded([&] {
+    require(c && host && n_tasks, MMC_ERR_INVALID, "null argument");
+    require(c->step_trace != nullptr, MMC_ERR_STATE, "no step trace (MMC_STEP_TRACE=1 at creation)");
+    use_device(c);
+    ck(cudaStreamSynchronize(c->stream), "sync");
+    const int64_t n = std::min<int64_t>(max_tasks, c->step_trace_tasks);
+    ck(cudaMemcpy(host, c->step_trace, size_t(n) * 8 * 8, cudaMemcpyDeviceToHost), "trace read");
+    *n_tasks = c->step_trace_tasks;
+  });
+}
+
 int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int32_t* tokens, int32_t* next_tokens,
                     float* logits_host) {
   return guarded([&] {
@@ -1422,6 +1591,12 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     io.slots = c->slots;
     io.tokens = c->tokens;
     io.logits = logits_host ? c->logits : nullptr;
+    if (!use_graph && !use_step(c, io)) {
+      fill_attn_order(c, io, seq_ids, c->h_order);
+      ck(cudaMemcpyAsync(c->attn_order, c->h_order, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream),
+         "H2D attention order");
+      io.order = c->attn_order;
+    }
     if (use_graph) {
       ck(cudaGraphLaunch(c->graph, c->stream), "graph launch");
     } else {
@@ -1638,6 +1813,11 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     io.hist = c->hist;
     io.hist_step = c->hist_step;
     io.hist_cap = c->hist_cap;
+    if (!use_step(c, io)) {  // the captured attention launches read this order on every replay
+      fill_attn_order(c, io, seq_ids, c->h_order);
+      upload(c, c->attn_order, c->h_order, sizeof(int) * batch, "attention order");
+      io.order = c->attn_order;
+    }
     cudaGraph_t g = nullptr;
     ck(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
     try {
@@ -1789,6 +1969,10 @@ int mmc_kernels_per_step(const mmc_ctx* c, int32_t batch, int32_t* k) {
   return guarded([&] {
     require(c && k, MMC_ERR_INVALID, "null argument");
     require(batch >= 1, MMC_ERR_INVALID, "bad batch");
+    if (c->lm_f != nullptr && c->step_sync != nullptr && batch <= kStepMaxRows) {  // the persistent step
+      *k = 1;
+      return;
+    }
     // a batch that runs as concurrent parts launches each part's chain
     const int P = batch > kGemvMaxBatch ? batch_parts(c, batch) : 1;
     int total = 0;
