@@ -129,7 +129,7 @@ MMC_EXPORT int mmc_debug_fill_kv(mmc_ctx* ctx, int32_t seq, int64_t n_tokens, ui
  * 3 SiLU*mul activations [batch][intermediate]. `count` floats are copied. */
 MMC_EXPORT int mmc_debug_scratch(mmc_ctx* ctx, int32_t which, float* host, int64_t count);
 
-/* Debug helper for the persistent step (batches of up to 64 rows): with
+/* Debug helper for the persistent step (MMC_PERSISTENT=1, batches of up to 64 rows): with
  * MMC_STEP_TRACE=1 set when the context was created, each step records per
  * task global-timer nanoseconds (CTA, start, dependencies met, computed,
  * signalled, three unused); this copies the last step's records ([n][8]
@@ -230,8 +230,9 @@ MMC_EXPORT int mmc_graph_stream_stop(mmc_ctx* ctx);
 /* Wait for the context's stream and report any device-side error. */
 MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
 /* Number of kernels one decode step launches for a batch of `batch` rows:
- * 1 for batches of up to 64 rows on dense models (the persistent step:
- * the whole step is one cooperative launch); otherwise 6 per layer + 1 for
+ * 1 for batches of up to 64 rows on dense models when the context was
+ * created with MMC_PERSISTENT=1 (the persistent step: the whole step is one
+ * cooperative launch); otherwise 6 per layer + 1 for
  * batch <= 4, and above, 6 per layer + 2 for each of the concurrent parts the
  * batch runs as (up to 4 parts of >= 64 rows). */
 MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* kernels);

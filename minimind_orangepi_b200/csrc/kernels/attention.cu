@@ -113,6 +113,10 @@ __device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, StageMeta&
   m.split = w / per_split;
   const int bh = w % per_split;
   m.b = a.order ? a.order[bh / a.nkv] : bh / a.nkv;
+  if (m.b < 0 || m.b >= a.B) {  // a corrupt order entry: record it, skip the item
+    set_error(a.err, kDevPositionLimit);
+    return false;
+  }
   m.h = bh % a.nkv;
   const int ctx = a.seq_pos[a.slots[m.b]] + (a.row_off ? a.row_off[m.b] : 0) + 1;
   const int pages = (ctx + kPageTokens - 1) / kPageTokens;

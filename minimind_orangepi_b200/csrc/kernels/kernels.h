@@ -234,6 +234,7 @@ struct StepArgs {
   __half* kv_pool = nullptr;
   const int* block_table = nullptr;
   int max_pages = 0;
+  int n_pages = 0;  // pages in the pool (page ids from the block table are checked against it)
   int* seq_pos = nullptr;
   const int* slots = nullptr;
   int* tokens = nullptr;    // [B] in: this step's tokens, out: next tokens

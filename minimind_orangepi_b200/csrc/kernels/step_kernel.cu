@@ -103,6 +103,10 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 
+// Self-checks of the indices the kernel derives (each records a distinct
+// code in the error word and the access is skipped).
+#define STEP_CHECK(cond, id) ((cond) ? true : (set_error(a.err, 100 + (id)), false))
+
 struct ArgBest {
   float v;
   int i;
@@ -286,7 +290,10 @@ __device__ void issue_prefetch(const StepArgs& a, const Task& k, const AttnGeo& 
   const int np = p1 - p0;
   int my_page = -1;
   if (lane < np) my_page = __ldcg(a.block_table + (size_t)geo.slot * a.max_pages + p0 + lane);
-  if (lane < np && my_page < 0) set_error(a.err, kDevNoPage);
+  if (lane < np && (my_page < 0 || my_page >= a.n_pages)) {  // unreserved (or corrupt) entry: skip the copy
+    set_error(a.err, kDevNoPage);
+    my_page = -1;
+  }
   if (lane == 0) mbar_arrive_expect_tx(bar, uint32_t(bytes));
   int missing = 0;
   for (int p = 0; p < np; ++p) {
@@ -342,7 +349,8 @@ __device__ __forceinline__ void issue_x_warp(const StepArgs& a, const Task& k, S
   __syncwarp();
   if (lane < k.nr) {
     fence_proxy_async_global();  // the rows were written (generic proxy) by other CTAs
-    bulk_g2s(xs + lane * XS, x + size_t(lane) * K, uint32_t(K * 2), &sh.x_bar);
+    if (STEP_CHECK(k.g * kStepGroupRows + k.r0 + lane < a.B && k.nr * XS <= kXHalves, 12))
+      bulk_g2s(xs + lane * XS, x + size_t(lane) * K, uint32_t(K * 2), &sh.x_bar);
   }
 }
 
@@ -383,6 +391,14 @@ __device__ void gemm_task(const StepArgs& a, const Task& k, Shared& sh, const ui
   wait_bar(&sh.slot_bar[slot], (par >> slot) & 1u, a, sh);
   par ^= 1u << slot;
   const uint4* wf = reinterpret_cast<const uint4*>(ring + sh.slot_off[slot]) + size_t(my_tile) * nk * 32;
+  {
+    AttnGeo none{};
+    const int bytes = entry_bytes(a, k, none, 0);
+    if (!STEP_CHECK(sh.slot_off[slot] >= 0 && sh.slot_off[slot] + bytes <= kRingBytes &&
+                        (my_tile + 1) * nk * 32 * 16 <= bytes && XS * 2 * (nt > 2 ? 32 : 16) <= kXBytes,
+                    14))
+      wf = reinterpret_cast<const uint4*>(ring);
+  }
   wait_bar(&sh.x_bar, xpar & 1u, a, sh);
   xpar ^= 1u;
   // two k-steps per iteration: both steps' loads before their mma
@@ -445,10 +461,10 @@ __device__ void gemm_task(const StepArgs& a, const Task& k, Shared& sh, const ui
     const int n = (tile0 + tt) * 16 + row;
     if (normed) y *= sh.rs[col];
     if (k.type == kQkv) {
-      if (ok) a.qkv[size_t(b) * a.NQKV + n] = y;
+      if (ok && STEP_CHECK(b < a.B && n < a.NQKV, 2)) a.qkv[size_t(b) * a.NQKV + n] = y;
     } else if (resid) {
       float hn = 0.f;
-      if (ok) {
+      if (ok && STEP_CHECK(b < a.B && n < a.H && tile0 + tt < a.H / 16, 3)) {
         const size_t i2 = size_t(b) * a.H + n;
         hn = hv[m] + y;
         a.h[i2] = hn;
@@ -461,7 +477,7 @@ __device__ void gemm_task(const StepArgs& a, const Task& k, Shared& sh, const ui
     } else if (k.type == kGu) {
       if (live) ysum[idx] = y;
     } else {  // kLm: logits and this tile's first maximum per row
-      if (ok && a.logits) a.logits[size_t(b) * a.V + n] = y;
+      if (ok && a.logits && STEP_CHECK(b < a.B && n < a.V, 9)) a.logits[size_t(b) * a.V + n] = y;
       float bv = ok ? y : -INFINITY;
       int bi = ok ? n : 0x7fffffff;
 #pragma unroll
@@ -481,7 +497,7 @@ __device__ void gemm_task(const StepArgs& a, const Task& k, Shared& sh, const ui
     for (int idx = tid; idx < T * 8 * kStepGroupRows; idx += kThreads) {
       const int tt = idx / (8 * kStepGroupRows), rem = idx % (8 * kStepGroupRows);
       const int col = rem / 8, row = rem % 8;
-      if (col < k.nr) {
+      if (col < k.nr && STEP_CHECK(b0 + col < a.B && (tile0 + tt) * 8 + row < a.I, 4)) {
         const float gv = ysum[(tt * kStepGroupRows + col) * 16 + row];
         const float uv = ysum[(tt * kStepGroupRows + col) * 16 + row + 8];
         a.act16[size_t(b0 + col) * a.I + (tile0 + tt) * 8 + row] = __float2half_rn((gv / (1.0f + expf(-gv))) * uv);
@@ -495,7 +511,8 @@ __device__ void gemm_task(const StepArgs& a, const Task& k, Shared& sh, const ui
         if (better(best[tt * kStepGroupRows + tid].v, best[tt * kStepGroupRows + tid].i, bb.v, bb.i))
           bb = best[tt * kStepGroupRows + tid];
       ArgBest* part = reinterpret_cast<ArgBest*>(a.lm_part);
-      part[(size_t(k.g) * a.tasks[kLm] + k.tg) * kStepGroupRows + k.r0 + tid] = bb;
+      if (STEP_CHECK(k.g < kStepMaxGroups && k.tg < a.tasks[kLm] && k.r0 + tid < kStepGroupRows, 8))
+        part[(size_t(k.g) * a.tasks[kLm] + k.tg) * kStepGroupRows + k.r0 + tid] = bb;
     }
   }
 }
@@ -647,6 +664,10 @@ __device__ void attn_task(const StepArgs& a, const Task& k, Shared& sh, const ui
     wait_bar(&sh.slot_bar[slot], (par >> slot) & 1u, a, sh);
     par ^= 1u << slot;
     __half* pages = const_cast<__half*>(reinterpret_cast<const __half*>(ring + sh.slot_off[slot]));
+    if (!STEP_CHECK(sh.slot_off[slot] >= 0 && sh.slot_off[slot] + (cp1 - cp0) * 4 * TILE <= kRingBytes &&
+                        cp1 > cp0 && cp1 - cp0 <= a.split_pages,
+                    1))
+      pages = reinterpret_cast<__half*>(const_cast<uint8_t*>(ring));
     if (q.last && cp1 == q.pages) {
       // the new K/V row: into the shared copy of the current page and into
       // the cache (after the page copy has landed, so the two never overlap)
@@ -657,7 +678,7 @@ __device__ void attn_task(const StepArgs& a, const Task& k, Shared& sh, const ui
         __half* sp = pages + size_t(cp1 - 1 - cp0) * 2 * TILE + kv * TILE + r * HD + swz_chunk(r, c, CPR) * 8;
         *reinterpret_cast<uint4*>(sp) = v;
         const int page = __ldcg(a.block_table + (size_t)q.slot * a.max_pages + q.pos / kPageTokens);
-        if (page >= 0) {
+        if (page >= 0 && page < a.n_pages) {
           __half* gp =
               a.kv_pool + page_slab(page, k.layer, a.L, kv, a.nkv, q.h, TILE) + r * HD + swz_chunk(r, c, CPR) * 8;
           *reinterpret_cast<uint4*>(gp) = v;
@@ -771,6 +792,7 @@ __device__ void attn_task(const StepArgs& a, const Task& k, Shared& sh, const ui
       Ls += cw[HD + 1] * f;
       O += cw[d] * f;
     }
+    if (!STEP_CHECK(q.b < a.B && q.h < a.nkv && q.s < a.s_max && j < rep, 5)) continue;
     if (q.nsplits == 1) {
       a.attn16[out_off + i] = __float2half_rn(O / Ls);
     } else {
@@ -877,11 +899,14 @@ __global__ void __launch_bounds__(kBlock, 1) step_kernel(const __grid_constant__
           }
           if (e - done < kSlots) {
             if (bytes == 0) break;
+            // live data occupies [free_pos, alloc) of the ring's linear address
+            // space (nothing when every issued entry has been consumed)
             const unsigned long long free_pos = done > 0 ? sh.slot_end[(done - 1) % kSlots] : 0ull;
             p = alloc;
             const unsigned long long off = p % kRingBytes;
             if (off + bytes > kRingBytes) p += kRingBytes - off;  // no region wraps around the end
-            if (p + bytes - free_pos <= kRingBytes) break;
+            const unsigned long long live_start = free_pos >= alloc ? p : free_pos;
+            if (p + bytes - live_start <= kRingBytes) break;
           }
           if (ld_volatile(abort_p) != 0u || global_timer_ns() - t0 > 2000000000ull) {
             if (lane == 0) set_error(a.err, kDevWaitTimeout);
@@ -891,6 +916,11 @@ __global__ void __launch_bounds__(kBlock, 1) step_kernel(const __grid_constant__
           __nanosleep(32);
         }
         if (!ok) break;
+        if (bytes > kRingBytes || int(p % kRingBytes) + bytes > kRingBytes) {  // never: the plan caps entries
+          if (lane == 0) set_error(a.err, kDevWaitTimeout);
+          ok = false;
+          break;
+        }
         if (bytes > 0) {
           if (lane == 0) sh.slot_off[s] = int(p % kRingBytes);
           __syncwarp();

@@ -153,7 +153,7 @@ struct mmc_ctx {
   bool mlp_chain = false;  // MMC_MLP_CHAIN at creation
   float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
   // persistent step (batches of up to kStepMaxRows rows, dense models)
-  bool persistent = true;  // MMC_PERSISTENT at creation (default on)
+  bool persistent = false;  // MMC_PERSISTENT at creation (default off: measured slower than the chain)
   __half* lm_f = nullptr;
   float* step_ssp = nullptr;       // [rows][H / 16]
   float* step_part = nullptr;      // [rows][nkv][max_pages][rep][hd + 2]
@@ -227,7 +227,7 @@ void raise_device_error(mmc_ctx* c, int e) {
   if (e != 0) {
     ck(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream), "clear device error word");
     ck(cudaStreamSynchronize(c->stream), "clear device error word");
-    fail(MMC_ERR_DEVICE, std::string("device error: ") + device_error_text(e));
+    fail(MMC_ERR_DEVICE, std::string("device error: ") + device_error_text(e) + " (code " + std::to_string(e) + ")");
   }
 }
 
@@ -738,6 +738,7 @@ void enqueue_persistent(mmc_ctx* c, const StepIO& io, cudaStream_t s) {
   a.kv_pool = c->kv_pool;
   a.block_table = c->d_block_table;
   a.max_pages = c->max_pages;
+  a.n_pages = int(c->n_pages);
   a.seq_pos = c->d_seq_pos;
   a.slots = io.slots;
   a.tokens = io.tokens;
@@ -1189,7 +1190,7 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     ck(cudaEventCreateWithFlags(&c->fork_ev, cudaEventDisableTiming), "event");
     c->split_parts = std::max(1, std::min(kMaxParts, env_int("MMC_SPLIT_BATCH", 4)));
     c->mlp_chain = env_int("MMC_MLP_CHAIN", 0) != 0;
-    c->persistent = env_int("MMC_PERSISTENT", 1) != 0;
+    c->persistent = env_int("MMC_PERSISTENT", 0) != 0;
     c->step_trace_on = env_int("MMC_STEP_TRACE", 0) != 0;
     ck(mmc::step_init_attributes(), "persistent step attributes");
     ck(mmc::gemv_init_attributes(), "gemv attributes");
@@ -2175,7 +2176,7 @@ int mmc_op_attention_status(const void* ws, void* stream) {
     if (e != 0) {
       ck(cudaMemsetAsync(const_cast<void*>(ws), 0, sizeof(int), s), "clear attention error word");
       ck(cudaStreamSynchronize(s), "clear attention error word");
-      fail(MMC_ERR_DEVICE, std::string("device error: ") + device_error_text(e));
+      fail(MMC_ERR_DEVICE, std::string("device error: ") + device_error_text(e) + " (code " + std::to_string(e) + ")");
     }
   });
 }
