@@ -695,8 +695,9 @@ void part_rows(int B, int p, int i, int* r0, int* n) {
 // items (pages per split under the part's split plan), longest first, so the
 // persistent attention kernel hands out the long items before the short ones
 // and its tail is short. Fills host[0, B) with part-relative row indices.
-void fill_attn_order(const mmc_ctx* c, const StepIO& io, const int32_t* seq_ids, int* host) {
-  const int P = batch_parts(c, io.B);
+// With `whole`, the batch is one part (a step enqueued without splitting).
+void fill_attn_order(const mmc_ctx* c, const StepIO& io, const int32_t* seq_ids, int* host, bool whole = false) {
+  const int P = whole ? 1 : batch_parts(c, io.B);
   for (int i = 0; i < P; ++i) {
     int r0 = 0, n = io.B;
     if (P > 1) part_rows(io.B, P, i, &r0, &n);
@@ -1592,7 +1593,7 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     io.slots = c->slots;
     io.tokens = c->tokens;
     io.logits = logits_host ? c->logits : nullptr;
-    if (!use_graph && !use_step(c, io)) {
+    if (!use_graph && !use_step(c, io) && env_int("MMC_ATTN_ORDER", 1) != 0) {
       fill_attn_order(c, io, seq_ids, c->h_order);
       ck(cudaMemcpyAsync(c->attn_order, c->h_order, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream),
          "H2D attention order");
@@ -1725,6 +1726,11 @@ int mmc_profile_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const in
     c->async_slots.clear();
     io.slots = c->slots;
     io.tokens = c->tokens;
+    if (env_int("MMC_ATTN_ORDER", 1) != 0) {  // the profiled step runs the batch as one part
+      fill_attn_order(c, io, seq_ids, c->h_order, /*whole=*/true);
+      upload(c, c->attn_order, c->h_order, sizeof(int) * batch, "attention order");
+      io.order = c->attn_order;
+    }
     const int n = kernels_per_step(c, batch);
     std::vector<cudaEvent_t> ev(size_t(n) + 1);
     std::vector<int> kinds;
@@ -1814,7 +1820,7 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     io.hist = c->hist;
     io.hist_step = c->hist_step;
     io.hist_cap = c->hist_cap;
-    if (!use_step(c, io)) {  // the captured attention launches read this order on every replay
+    if (!use_step(c, io) && env_int("MMC_ATTN_ORDER", 1) != 0) {  // read by the captured attention launches
       fill_attn_order(c, io, seq_ids, c->h_order);
       upload(c, c->attn_order, c->h_order, sizeof(int) * batch, "attention order");
       io.order = c->attn_order;
