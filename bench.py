@@ -397,7 +397,10 @@ def main() -> None:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             try:
-                cpu = cpu_reference_sample(w, model_dir, max(1, min(os.cpu_count() or 1, 64)), None,
+                # batch-1 workloads: the reference decodes one sequence on one core
+                # (its CPU path is single-threaded); batched: one sequence per host thread
+                threads = 1 if w["n_seqs"] == 1 else max(1, min(os.cpu_count() or 1, 64))
+                cpu = cpu_reference_sample(w, model_dir, threads, None,
                                            args.cpu_seconds, lens)
             except Exception as e:  # keep the GPU line even if the CPU leg fails
                 cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "unavailable", "sample": str(e)}
