@@ -232,9 +232,10 @@ MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
 /* Number of kernels one decode step launches for a batch of `batch` rows:
  * 1 for batches of up to 64 rows on dense models when the context was
  * created with MMC_PERSISTENT=1 (the persistent step: the whole step is one
- * cooperative launch); otherwise 6 per layer + 1 for
- * batch <= 4, and above, 6 per layer + 2 for each of the concurrent parts the
- * batch runs as (up to 4 parts of >= 64 rows). */
+ * cooperative launch); otherwise 5 per layer + 1 for
+ * batch <= 4, and above, 5 per layer + 2 for each of the concurrent parts the
+ * batch runs as (up to 4 parts of >= 64 rows); one more per layer when the
+ * context was created with MMC_ATTN_FUSED=0 (separate q/k prep launch). */
 MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* kernels);
 
 /* ------------------------------------------------------------- single ops

@@ -61,9 +61,17 @@ struct AttnCfg {
   static constexpr size_t STAGE_BYTES = size_t(2) * TILE * 2;
   static constexpr size_t RING_BYTES = NST * STAGE_BYTES;
   // per stage: the group's q heads; after the ring: warp partials [warps][rep][HD + 2]
-  __host__ __device__ static size_t q_bytes(int rep) { return size_t(rep) * HD * 2; }
+  // per stage: the group's fp16 q heads (prepared by qk_prep_kernel), or,
+  // fused, the raw fp32 q heads and the raw k and v of the group's kv head
+  __host__ __device__ static size_t q_bytes(int rep, bool fused) {
+    return fused ? size_t(rep + 2) * HD * 4 : size_t(rep) * HD * 2;
+  }
   __host__ __device__ static size_t comb_floats(int rep) { return size_t(kConsumerWarps) * rep * (HD + 2); }
-  __host__ __device__ static size_t smem(int rep) { return RING_BYTES + NST * q_bytes(rep) + comb_floats(rep) * 4; }
+  // fused: the item's normalised + rotated q heads and new k, v rows (fp16)
+  __host__ __device__ static size_t prep_bytes(int rep, bool fused) { return fused ? size_t(rep + 2) * HD * 2 : 0; }
+  __host__ __device__ static size_t smem(int rep, bool fused) {
+    return RING_BYTES + NST * q_bytes(rep, fused) + comb_floats(rep) * 4 + prep_bytes(rep, fused);
+  }
 };
 
 __device__ __forceinline__ size_t page_slab(int page, int layer, int layers, int kv, int nkv, int h, int tile) {
@@ -103,6 +111,8 @@ __device__ __forceinline__ void norm_rope_head(const float* src, const float* w,
 
 struct StageMeta {
   int b, h, split, tok_begin, tok_end, nch, nsplits, chunk;  // chunk < 0: end of this CTA's stream
+  int pos;   // the row's current position (ctx - 1)
+  int page;  // the page this stage holds
 };
 
 // Work item w (split-major numbering). A sequence of P cached pages is cut into
@@ -119,6 +129,11 @@ __device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, StageMeta&
   }
   m.h = bh % a.nkv;
   const int ctx = a.seq_pos[a.slots[m.b]] + (a.row_off ? a.row_off[m.b] : 0) + 1;
+  m.pos = ctx - 1;
+  if (a.fused && (ctx > a.max_pos || (ctx - 1) / kPageTokens >= a.max_pages)) {
+    set_error(a.err, kDevPositionLimit);
+    return false;
+  }
   const int pages = (ctx + kPageTokens - 1) / kPageTokens;
   const int split_pages = a.split_tokens / kPageTokens;
   m.nsplits = (pages + split_pages - 1) / split_pages;
@@ -194,7 +209,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
   __half* ring = reinterpret_cast<__half*>(smem);
   const int rep = a.nq / a.nkv;
   __half* qring = reinterpret_cast<__half*>(smem + C::RING_BYTES);                        // [NST][rep][HD]
-  float* comb = reinterpret_cast<float*>(smem + C::RING_BYTES + C::NST * C::q_bytes(rep));  // [warps][rep][HD+2]
+  float* comb = reinterpret_cast<float*>(smem + C::RING_BYTES + C::NST * C::q_bytes(rep, a.fused));  // [warps][rep][HD+2]
+  __half* prep = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(comb) + C::comb_floats(rep) * 4);  // [rep+2][HD]
+  const size_t qstride = C::q_bytes(rep, a.fused) / 2;  // halves per q stage
   __shared__ __align__(8) uint64_t full_bar[C::NST];
   __shared__ __align__(8) uint64_t empty_bar[C::NST];
   __shared__ StageMeta meta[C::NST];
@@ -291,18 +308,31 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
       if (lane == 0) {
         StageMeta m = cur;
         m.chunk = chunk;
+        m.page = page;
         meta[s] = m;
         const bool first = chunk == 0;
-        const uint32_t qbytes = uint32_t(rep * HD * 2);
+        const bool last_split = cur.tok_end == cur.pos + 1;
+        // fused: raw q heads, plus raw k and v for the split holding the current position
+        const uint32_t qbytes = a.fused ? uint32_t((rep + (last_split ? 2 : 0)) * HD * 4) : uint32_t(rep * HD * 2);
         mbar_arrive_expect_tx(&full_bar[s], uint32_t(C::STAGE_BYTES) + (first ? qbytes : 0u));
         __half* dst = ring + (size_t)s * 2 * C::TILE;
         bulk_g2s(dst, a.kv_pool + page_slab(page, a.layer, a.layers, 0, a.nkv, cur.h, C::TILE), C::TILE * 2,
                  &full_bar[s]);
         bulk_g2s(dst + C::TILE, a.kv_pool + page_slab(page, a.layer, a.layers, 1, a.nkv, cur.h, C::TILE),
                  C::TILE * 2, &full_bar[s]);
-        if (first)
-          bulk_g2s(qring + (size_t)s * rep * HD, a.q16 + ((size_t)cur.b * a.nq + cur.h * rep) * HD, qbytes,
+        if (first && a.fused) {
+          float* raw = reinterpret_cast<float*>(qring + (size_t)s * qstride);
+          const float* row = a.qkv + (size_t)cur.b * a.ld_qkv;
+          bulk_g2s(raw, row + (size_t)cur.h * rep * HD, uint32_t(rep * HD * 4), &full_bar[s]);
+          if (last_split) {
+            bulk_g2s(raw + rep * HD, row + (size_t)(a.nq + cur.h) * HD, uint32_t(HD * 4), &full_bar[s]);
+            bulk_g2s(raw + (rep + 1) * HD, row + (size_t)(a.nq + a.nkv + cur.h) * HD, uint32_t(HD * 4),
+                     &full_bar[s]);
+          }
+        } else if (first) {
+          bulk_g2s(qring + (size_t)s * qstride, a.q16 + ((size_t)cur.b * a.nq + cur.h * rep) * HD, qbytes,
                    &full_bar[s]);
+        }
       }
       __syncwarp();
       ++chunk;
@@ -334,7 +364,25 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
       const __half* vt = kt + C::TILE;
       if (m.chunk == 0) {  // a new item: its q heads arrived with this page
         it = m;
-        const __half* qs = qring + (size_t)s * rep * HD;
+        const __half* qs = qring + (size_t)s * qstride;
+        if (a.fused) {
+          // q/k per-head RMSNorm + RoPE (decoder_layer.cpp:342-359) from the raw
+          // projections in this stage: q heads for the item, and the new k and
+          // v rows when the item holds the current position. (Every warp has
+          // its previous item's q in registers: the merge synchronised them.)
+          const float* raw = reinterpret_cast<const float*>(qs);
+          const float* cos_r = a.rope_cos + (size_t)it.pos * (HD / 2);
+          const float* sin_r = a.rope_sin + (size_t)it.pos * (HD / 2);
+          for (int j = warp; j < rep; j += kConsumerWarps)
+            norm_rope_head<HD>(raw + j * HD, a.q_norm, cos_r, sin_r, a.eps, prep + j * HD, lane);
+          if (it.tok_end == it.pos + 1) {
+            if (warp == 0) norm_rope_head<HD>(raw + rep * HD, a.k_norm, cos_r, sin_r, a.eps, prep + rep * HD, lane);
+            if (warp == 1)
+              for (int d = lane; d < HD; d += 32) prep[(rep + 1) * HD + d] = __float2half_rn(raw[(rep + 1) * HD + d]);
+          }
+          consumer_sync();
+          qs = prep;
+        }
 #pragma unroll
         for (int kc = 0; kc < C::KC; ++kc) {
           qb0[kc] = g < rep ? *reinterpret_cast<const uint32_t*>(qs + g * HD + 16 * kc + 2 * t) : 0u;
@@ -344,6 +392,22 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
         lA = lB = 0.f;
 #pragma unroll
         for (int mt = 0; mt < C::KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      }
+      if (a.fused && m.chunk == it.nch - 1 && it.tok_end == it.pos + 1) {
+        // the new K/V row: into this stage's copy of the current page (the
+        // copy predates it) and into the cache for later steps (the K/V
+        // append of the reference, decoder_layer.cpp:355-359)
+        const int r = it.pos % kPageTokens;
+        if (tid < 2 * C::CPR) {
+          const int kv = tid / C::CPR, ch = tid % C::CPR;
+          const uint4 v = *reinterpret_cast<const uint4*>(prep + (rep + kv) * HD + ch * 8);
+          __half* sp = ring + (size_t)s * 2 * C::TILE + kv * C::TILE + r * HD + swz_chunk(r, ch, C::CPR) * 8;
+          *reinterpret_cast<uint4*>(sp) = v;
+          __half* gp = a.kv_pool + page_slab(m.page, a.layer, a.layers, kv, a.nkv, it.h, C::TILE) + (size_t)r * HD +
+                       swz_chunk(r, ch, C::CPR) * 8;
+          *reinterpret_cast<uint4*>(gp) = v;
+        }
+        consumer_sync();
       }
       const int tok0 = it.tok_begin + m.chunk * kPageTokens + r0;
       if (tok0 < it.tok_end) {
@@ -556,8 +620,10 @@ cudaError_t launch_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
   prep.stream = s;
   prep.attrs = attr;
   prep.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&prep, qk_prep_kernel<HD>, a);
-  if (e != cudaSuccess) return e;
+  if (!a.fused) {
+    const cudaError_t e = cudaLaunchKernelEx(&prep, qk_prep_kernel<HD>, a);
+    if (e != cudaSuccess) return e;
+  }
   cudaLaunchConfig_t cfg = {};
   const int items = a.max_splits * a.nkv * a.B;
   int dev = 0, sms = 148;
@@ -566,17 +632,17 @@ cudaError_t launch_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
   const int per_sm = a.ctas_per_sm > 0 ? a.ctas_per_sm : 2;
   cfg.gridDim = dim3(items < per_sm * sms ? items : per_sm * sms);
   cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = AttnCfg<HD>::smem(a.nq / a.nkv);
+  cfg.dynamicSmemBytes = AttnCfg<HD>::smem(a.nq / a.nkv, a.fused != 0);
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;  // always overlaps qk_prep_kernel's tail
+  cfg.numAttrs = (pdl || !a.fused) ? 1 : 0;  // unfused: always overlaps qk_prep_kernel's tail
   return cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
 }
 
 template <int HD>
 cudaError_t attr_hd() {
   return cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(AttnCfg<HD>::smem(kMaxRep)));
+                              int(AttnCfg<HD>::smem(kMaxRep, true)));
 }
 
 }  // namespace
@@ -597,7 +663,8 @@ cudaError_t attention_init_attributes() {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   if (a.nkv <= 0 || a.nq % a.nkv != 0 || a.nq / a.nkv > kMaxRep || a.split_tokens % kPageTokens != 0 ||
-      a.max_splits <= 0 || a.B <= 0 || a.work == nullptr || a.q16 == nullptr)
+      a.max_splits <= 0 || a.B <= 0 || a.work == nullptr || (a.q16 == nullptr && !a.fused) ||
+      (a.fused && a.row_off != nullptr))
     return cudaErrorInvalidValue;
   switch (a.hd) {
     case 16: return launch_hd<16>(a, s, pdl);

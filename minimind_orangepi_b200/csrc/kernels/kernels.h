@@ -184,6 +184,11 @@ struct AttnArgs {
   const int* slots = nullptr;    // [B]
   const int* row_off = nullptr;  // optional [B]: row b sits at seq_pos[slots[b]] + row_off[b] (prompt pass)
   const int* order = nullptr;    // optional [B]: work-queue order of the rows (longest work items first)
+  // fused (decode steps: one row per sequence): the attention kernel does the
+  // q/k RMSNorm + RoPE and the K/V append itself from the raw projections, and
+  // the prep launch is skipped (a prompt pass, whose rows read each other's
+  // appended rows, keeps the prep launch)
+  int fused = 0;
   int B = 0, nq = 0, nkv = 0, hd = 0;
   int split_tokens = 0;  // multiple of the page size
   int max_splits = 0;    // grid.x

@@ -151,6 +151,7 @@ struct mmc_ctx {
   unsigned* chain_sync = nullptr;  // [parts][chain_sync_words(max_batch)] projection-chain queues
   int chain_words = 0;
   bool mlp_chain = false;  // MMC_MLP_CHAIN at creation
+  bool attn_fused = true;  // MMC_ATTN_FUSED at creation: q/k prep inside the decode attention launch
   float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
   // persistent step (batches of up to kStepMaxRows rows, dense models)
   bool persistent = false;  // MMC_PERSISTENT at creation (default off: measured slower than the chain)
@@ -295,8 +296,19 @@ enum Kind { kKindQkv = 0, kKindAttn = 1, kKindO = 2, kKindGateUp = 3, kKindDown 
 // so it is off by default.
 bool use_mlp_chain(const mmc_ctx* c) { return c->mlp_chain; }
 
-int kernels_per_step(const mmc_ctx* c, int B) {
+// `alone`: the batch runs as one part (the decode attention then folds the
+// q/k prep into its own launch; concurrent parts keep the separate prep
+// launch, measured faster there)
+int kernels_per_step(const mmc_ctx* c, int B, bool alone = true) {
   const int L = int(c->d.num_hidden_layers);
+  if (c->attn_fused && alone) {  // attention is one launch (q/k prep fused in)
+    if (c->moe_experts > 0) {
+      const int per = 4 + 2 * c->moe_experts;
+      return B <= kGemvMaxBatch ? per * L + 1 : per * L + 2;
+    }
+    if (B <= kGemvMaxBatch) return 5 * L + 1;
+    return (use_mlp_chain(c) ? 3 : 5) * L + 2;
+  }
   // attention is two launches; the tensor-core path adds the layer-0
   // embedding gather (its RMSNorms are folded into the projections)
   if (c->moe_experts > 0) {  // o, router and gate/up + down per expert replace the dense MLP
@@ -448,6 +460,8 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     a.seq_pos = c->d_seq_pos;
     a.row_off = io.row_off;
     a.order = io.order ? io.order + io.row0 : nullptr;
+    // decode steps of a batch running alone: q/k prep inside the attention kernel
+    a.fused = io.row_off == nullptr && c->attn_fused && io.alone;
     a.slots = io.slots;
     a.B = io.B;
     a.nq = int(d.num_attention_heads);
@@ -1192,6 +1206,7 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     c->split_parts = std::max(1, std::min(kMaxParts, env_int("MMC_SPLIT_BATCH", 4)));
     c->mlp_chain = env_int("MMC_MLP_CHAIN", 0) != 0;
     c->persistent = env_int("MMC_PERSISTENT", 0) != 0;
+    c->attn_fused = env_int("MMC_ATTN_FUSED", 1) != 0;
     c->step_trace_on = env_int("MMC_STEP_TRACE", 0) != 0;
     ck(mmc::step_init_attributes(), "persistent step attributes");
     ck(mmc::gemv_init_attributes(), "gemv attributes");
@@ -1986,7 +2001,7 @@ int mmc_kernels_per_step(const mmc_ctx* c, int32_t batch, int32_t* k) {
     for (int i = 0; i < P; ++i) {
       int r0 = 0, n = batch;
       if (P > 1) part_rows(batch, P, i, &r0, &n);
-      total += kernels_per_step(c, n);
+      total += kernels_per_step(c, n, P == 1);
     }
     *k = total;
   });
