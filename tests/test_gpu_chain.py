@@ -31,7 +31,7 @@ def engine(d, chain: bool, n):
             os.environ["MMC_MLP_CHAIN"] = old
 
 
-@pytest.mark.parametrize("shape_name,n", [("minimind2-small", 100), ("minimind2", 200)])
+@pytest.mark.parametrize("shape_name,n", [("minimind2-small", 100), ("minimind2", 256)])
 def test_chain_matches_separate_projections(shape_name, n):
     shape = SHAPES[shape_name]
     d = write_runtime_model(Path("/tmp/mmc_test_models") / f"chain-{shape_name}", shape, 9, eps=1e-5, theta=1e6)
