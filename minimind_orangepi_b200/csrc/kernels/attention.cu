@@ -263,8 +263,34 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
     StageMeta cur{}, nxt{};
     bool have_cur = fetch(cur), have_nxt = false, nxt_decoded = false;
     int cur_pages = have_cur ? load_pages(cur, 0) : -1, nxt_pages = -1;
-    pdl_wait();
-    pdl_launch_dependents();
+    // Fused, the cached pages do not depend on the previous kernel (the
+    // current position's row is patched in by the consumers): the first
+    // item's pages go out before the dependency wait, and only its raw q/k/v
+    // copy waits for the q|k|v projection to finish.
+    bool waited = !a.fused;
+    if (waited) {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    int def_stage = -1;  // stage whose raw q/k/v copy waits for the dependency
+    StageMeta def_item{};
+    auto issue_raw = [&](int st, const StageMeta& it) {  // lane 0
+      float* raw = reinterpret_cast<float*>(qring + (size_t)st * qstride);
+      const float* row = a.qkv + (size_t)it.b * a.ld_qkv;
+      bulk_g2s(raw, row + (size_t)it.h * rep * HD, uint32_t(rep * HD * 4), &full_bar[st]);
+      if (it.tok_end == it.pos + 1) {
+        bulk_g2s(raw + rep * HD, row + (size_t)(a.nq + it.h) * HD, uint32_t(HD * 4), &full_bar[st]);
+        bulk_g2s(raw + (rep + 1) * HD, row + (size_t)(a.nq + a.nkv + it.h) * HD, uint32_t(HD * 4), &full_bar[st]);
+      }
+    };
+    auto finish_wait = [&]() {  // whole warp
+      if (waited) return;
+      pdl_wait();
+      pdl_launch_dependents();
+      waited = true;
+      if (lane == 0 && def_stage >= 0) issue_raw(def_stage, def_item);
+      __syncwarp();
+    };
     int chunk = 0;
     bool done = !have_cur;
     for (int c = 0;; ++c) {
@@ -321,13 +347,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
         bulk_g2s(dst + C::TILE, a.kv_pool + page_slab(page, a.layer, a.layers, 1, a.nkv, cur.h, C::TILE),
                  C::TILE * 2, &full_bar[s]);
         if (first && a.fused) {
-          float* raw = reinterpret_cast<float*>(qring + (size_t)s * qstride);
-          const float* row = a.qkv + (size_t)cur.b * a.ld_qkv;
-          bulk_g2s(raw, row + (size_t)cur.h * rep * HD, uint32_t(rep * HD * 4), &full_bar[s]);
-          if (last_split) {
-            bulk_g2s(raw + rep * HD, row + (size_t)(a.nq + cur.h) * HD, uint32_t(HD * 4), &full_bar[s]);
-            bulk_g2s(raw + (rep + 1) * HD, row + (size_t)(a.nq + a.nkv + cur.h) * HD, uint32_t(HD * 4),
-                     &full_bar[s]);
+          if (waited) {
+            issue_raw(s, cur);
+          } else {
+            def_stage = s;
+            def_item = cur;
           }
         } else if (first) {
           bulk_g2s(qring + (size_t)s * qstride, a.q16 + ((size_t)cur.b * a.nq + cur.h * rep) * HD, qbytes,
@@ -341,7 +365,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
         nxt_pages = have_nxt ? load_pages(nxt, 0) : -1;
         nxt_decoded = true;
       }
+      // the ring is full or the first item's pages are all out: now wait
+      if (!waited && (c + 1 >= C::NST || chunk >= cur.nch)) finish_wait();
     }
+    finish_wait();
     __syncwarp();
   } else {
     // ====================================================== consumer warps
