@@ -290,7 +290,7 @@ def main() -> None:
     lens, prompts = workload_prompts(w)
     K, W = args.steps, args.warmup
     E = K  # end-to-end steps through the host-buffer C ABI
-    need = [n + W + K + E + 2 for n in lens]
+    need = [n + W + K + E + K + 2 for n in lens]  # + K streamed steps
     shards = plan_shards(need, world)
     mine = shards[rank]
     B = len(mine)
@@ -353,6 +353,13 @@ def main() -> None:
     for _ in range(E):
         toks, _ = eng.step(seqs, toks)
     e2e_s = time.perf_counter() - t0
+    # ---------------- streamed: the device loop with each step's tokens read on the host as it lands
+    # (mmc_graph_stream_*: what generate_stream and --stream use), host wall clock
+    eng.graph_set_tokens(toks)
+    t0 = time.perf_counter()
+    for _ in eng.graph_stream(K):
+        pass
+    stream_s = time.perf_counter() - t0
     clocks = sampler.stop()
 
     # ---------------- per-kernel attribution (profiled steps, events between kernels)
@@ -430,6 +437,9 @@ def main() -> None:
                 "prefill_s_untimed": round(prefill_s, 2),
                 "prompt_pass": "synthetic K/V fast-forward" if args.fill_context else "device prompt pass (mmc_prefill)",
             },
+            "stream": {"value": w["n_seqs"] * K / stream_s, "unit": "tokens/s",
+                       "path": "graph replays whose lm_head epilogue writes each step's tokens to mapped pinned host memory, read by the host "
+                               "as they land (host wall clock, rank 0)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 8 * w["n_seqs"],
                     "d2h_bytes_per_step": 4 * w["n_seqs"],
                     "path": "mmc_decode_step (host token/sequence buffers -> pinned staging -> H2D, "

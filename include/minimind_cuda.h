@@ -203,8 +203,8 @@ MMC_EXPORT int mmc_decode_step_async(mmc_ctx* ctx, int32_t batch, const int32_t*
  * for this batch composition as a CUDA graph whose next tokens feed the
  * following step's embedding on the device. mmc_graph_run replays it
  * `n_steps` times (positions advance, pages must already be reserved) and
- * records every step's tokens on the device; mmc_graph_tokens copies them
- * out ([n_steps][batch]). */
+ * records every step's tokens in mapped pinned host memory; mmc_graph_tokens
+ * waits for the stream and copies them out ([n_steps][batch]). */
 MMC_EXPORT int mmc_graph_build(mmc_ctx* ctx, int32_t batch, const int32_t* seq_ids);
 MMC_EXPORT int mmc_graph_set_tokens(mmc_ctx* ctx, const int32_t* tokens_host);
 MMC_EXPORT int mmc_graph_run(mmc_ctx* ctx, int32_t n_steps, void* stream);
@@ -217,9 +217,14 @@ MMC_EXPORT int mmc_graph_tokens(mmc_ctx* ctx, int32_t n_steps, int32_t* tokens_h
  * mmc_graph_build (tokens set by mmc_graph_set_tokens); each
  * mmc_graph_stream_next returns the next step's tokens ([batch], host
  * memory) as soon as that step has finished on the device, while up to 32
- * later replays are already queued behind it. Each replay is followed by an
- * async copy of its tokens into a pinned ring, so the loop keeps running on
- * the device between reads. A position advances when its replay is queued;
+ * later replays are already queued behind it. The lm_head epilogue writes
+ * each step's tokens straight into mapped pinned host memory (a ring of 8192
+ * steps), so nothing but the replays runs on the stream and the loop keeps
+ * running on the device between reads. The device error word is copied back
+ * after every 8th replay and after the last one: a device-side error is
+ * reported by the next call of mmc_graph_stream_next that reaches such a
+ * replay (tokens of up to 7 steps before it may come from the failed steps),
+ * and always by the final one. A position advances when its replay is queued;
  * mmc_graph_stream_stop (or any other step, prompt pass or graph call) waits
  * for the queued replays and ends the run early, e.g. at an end-of-sequence
  * token. */

@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kThreads) gemm_tc_kernel(const __grid_constant
       if (s.seq_pos) s.seq_pos[s.slots[b]] += 1;
       if (s.hist) {
         const int step = *s.hist_step;
-        if (step < s.hist_cap) s.hist[step * s.hist_stride + b] = next;
+        s.hist[(step % s.hist_cap) * s.hist_stride + b] = next;  // a ring
       }
     }
   }

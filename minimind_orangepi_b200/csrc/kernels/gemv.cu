@@ -38,7 +38,7 @@ __device__ __forceinline__ void finalize_token(const TokenSink& s, int B, int b,
   if (s.seq_pos) s.seq_pos[s.slots[b]] += 1;
   if (s.hist) {
     const int step = *s.hist_step;
-    if (step < s.hist_cap) s.hist[step * s.hist_stride + b] = next;
+    s.hist[(step % s.hist_cap) * s.hist_stride + b] = next;  // a ring
   }
 }
 

@@ -551,7 +551,7 @@ __device__ void lm_finish(const StepArgs& a, const Shared& sh, const Task& k) {
       a.seq_pos[sh.row_slot[b]] = sh.row_pos[b] + 1;
       if (a.hist) {
         const int step = *(volatile int*)a.hist_step;
-        if (step < a.hist_cap) a.hist[size_t(step) * a.hist_stride + b] = next;
+        a.hist[size_t(step % a.hist_cap) * a.hist_stride + b] = next;  // a ring
       }
     }
   }

@@ -181,7 +181,8 @@ struct mmc_ctx {
 
   // streamed graph loop: each replay is followed by an async copy of its
   // tokens (and the device error word) into a pinned ring slot and an event
-  int* h_ring = nullptr;  // pinned [kRingSlots][max_batch + 1]
+  int* h_ring = nullptr;  // pinned [kRingSlots]: the device error word, copied after every 8th streamed step
+  int* h_hist = nullptr;  // host view of `hist` (mapped pinned memory the token sink writes directly)
   cudaEvent_t ring_ev[kRingSlots] = {};
   int64_t st_total = 0, st_enqueued = 0, st_consumed = 0;
 
@@ -1231,6 +1232,7 @@ void mmc_destroy(mmc_ctx* c) {
   if (c->h_stage) cudaFreeHost(c->h_stage);
   if (c->h_order) cudaFreeHost(c->h_order);
   if (c->h_ring) cudaFreeHost(c->h_ring);
+  if (c->h_hist) cudaFreeHost(c->h_hist);
   for (auto e : c->ring_ev)
     if (e) cudaEventDestroy(e);
   for (auto ps : c->part_stream)
@@ -1827,8 +1829,14 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     io.total_pages = total_pages;
     io.max_ctx = cap;
     if (!c->hist) {
+      // the history lives in mapped pinned host memory: the lm_head argmax
+      // epilogue writes each step's tokens straight to the host, so a
+      // streamed run needs no copy between graph replays
       c->hist_cap = 8192;
-      c->hist = c->alloc<int>(size_t(c->hist_cap) * c->max_batch, "token history");
+      ck(cudaHostAlloc(reinterpret_cast<void**>(&c->h_hist), sizeof(int) * size_t(c->hist_cap) * c->max_batch,
+                       cudaHostAllocMapped),
+         "token history (mapped)");
+      ck(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->hist), c->h_hist, 0), "token history device view");
       c->hist_step = c->alloc<int>(kMaxParts, "history counters (per batch part)");
     }
     upload(c, c->slots, seq_ids, sizeof(int) * batch, "slots");
@@ -1910,9 +1918,8 @@ int mmc_graph_stream_start(mmc_ctx* c, int32_t n_steps) {
               "position exceeds max_position_embeddings");
     }
     if (!c->h_ring) {
-      ck(cudaHostAlloc(reinterpret_cast<void**>(&c->h_ring), sizeof(int) * kRingSlots * (c->max_batch + 1),
-                       cudaHostAllocDefault),
-         "pinned token ring");
+      ck(cudaHostAlloc(reinterpret_cast<void**>(&c->h_ring), sizeof(int) * kRingSlots, cudaHostAllocDefault),
+         "pinned error words");
       for (auto& e : c->ring_ev) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "ring event");
     }
     ck(cudaMemsetAsync(c->hist_step, 0, kMaxParts * sizeof(int), c->stream), "history reset");
@@ -1921,16 +1928,17 @@ int mmc_graph_stream_start(mmc_ctx* c, int32_t n_steps) {
 }
 
 namespace {
-// keep up to kRingSlots replays (and their token copies) in flight ahead of
-// the host's reads; positions advance as each replay is enqueued
+// keep up to kRingSlots replays in flight ahead of the host's reads (each
+// replay's tokens land in the mapped history; an event marks its end, and
+// every 8th replay also copies the device error word); positions advance as
+// each replay is enqueued
 void stream_top_up(mmc_ctx* c) {
-  const int B = c->graph_batch;
   while (c->st_enqueued < c->st_total && c->st_enqueued < c->st_consumed + kRingSlots) {
     const int slot = int(c->st_enqueued % kRingSlots);
-    int* row = c->h_ring + size_t(slot) * (c->max_batch + 1);
     ck(cudaGraphLaunch(c->graph, c->stream), "graph launch");
-    ck(cudaMemcpyAsync(row, c->tokens, sizeof(int) * B, cudaMemcpyDeviceToHost, c->stream), "D2H step tokens");
-    ck(cudaMemcpyAsync(row + B, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H error word");
+    c->h_ring[slot] = 0;
+    if (c->st_enqueued % 8 == 7 || c->st_enqueued + 1 == c->st_total)
+      ck(cudaMemcpyAsync(c->h_ring + slot, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H error word");
     ck(cudaEventRecord(c->ring_ev[slot], c->stream), "ring event");
     for (int s : c->graph_slots) c->h_pos[s] += 1;
     ++c->st_enqueued;
@@ -1947,11 +1955,12 @@ int mmc_graph_stream_next(mmc_ctx* c, int32_t* tokens) {
     const int slot = int(c->st_consumed % kRingSlots);
     ck(cudaEventSynchronize(c->ring_ev[slot]), "streamed step");
     const int B = c->graph_batch;
-    const int* row = c->h_ring + size_t(slot) * (c->max_batch + 1);
-    if (row[B] != 0) {
+    if (c->h_ring[slot] != 0) {
+      const int e = c->h_ring[slot];
       stream_drain(c);
-      raise_device_error(c, row[B]);
+      raise_device_error(c, e);
     }
+    const int* row = c->h_hist + size_t(c->st_consumed % c->hist_cap) * B;
     std::memcpy(tokens, row, sizeof(int) * B);
     ++c->st_consumed;
     if (c->st_consumed == c->st_total) c->st_total = c->st_enqueued = c->st_consumed = 0;
@@ -1976,8 +1985,7 @@ int mmc_graph_tokens(mmc_ctx* c, int32_t n_steps, int32_t* tokens) {
     ck(cudaStreamSynchronize(c->stream), "sync");
     ck(cudaDeviceSynchronize(), "sync");
     check_device_error(c);
-    ck(cudaMemcpy(tokens, c->hist, sizeof(int) * size_t(n_steps) * c->graph_batch, cudaMemcpyDeviceToHost),
-       "history read");
+    std::memcpy(tokens, c->h_hist, sizeof(int) * size_t(n_steps) * c->graph_batch);
   });
 }
 

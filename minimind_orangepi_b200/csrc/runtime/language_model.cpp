@@ -256,7 +256,7 @@ void LanguageModel::generate_stream(const std::vector<int32_t>& prompt_tokens, i
   }
   // Longer runs stay on the captured device loop: the graph feeds each
   // step's token to the next on the device, and every step's token reaches
-  // the host through a pinned ring as soon as that step finishes, so the
+  // the host through mapped pinned memory as soon as that step finishes, so the
   // callback sees tokens while later steps are already running.
   mmc_ctx* ctx = device_->ctx();
   const int32_t seq = state.device->id();
