@@ -39,6 +39,7 @@ CUDA_SOURCES = [
     CSRC / "kernels" / "attention.cu",
     CSRC / "kernels" / "pack.cu",
     CSRC / "kernels" / "step_kernel.cu",
+    CSRC / "kernels" / "skinny.cu",
     CSRC / "mmc_api.cu",
     CSRC / "attention_noalloc.cu",
 ]

@@ -668,8 +668,9 @@ cudaError_t launch_hd(const AttnArgs& a, cudaStream_t s, bool pdl) {
 
 template <int HD>
 cudaError_t attr_hd() {
-  return cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(AttnCfg<HD>::smem(kMaxRep, true)));
+  const cudaError_t e = set_kernel_smem(qk_prep_kernel<HD>, 0);
+  const cudaError_t e2 = set_kernel_smem(attention_kernel<HD>, int(AttnCfg<HD>::smem(kMaxRep, true)));
+  return e != cudaSuccess ? e : e2;
 }
 
 }  // namespace

@@ -150,4 +150,17 @@ __device__ __forceinline__ int swz_chunk(int row, int chunk, int cpr) {
   return chunk ^ x;
 }
 
+
+// Host: a kernel's dynamic shared memory limit, and the full shared-memory
+// carveout for every kernel of the decode chain, so that consecutive kernels
+// never need an SM reconfiguration (which would keep a dependent launch's
+// CTAs off an SM until the previous kernel drained it).
+template <typename Kernel>
+inline cudaError_t set_kernel_smem(Kernel k, int dyn_bytes) {
+  const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_bytes);
+  const cudaError_t e2 =
+      cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+  return e != cudaSuccess ? e : e2;
+}
+
 }  // namespace mmc

@@ -522,17 +522,15 @@ template <int BN>
 cudaError_t attrs_bn() {
   cudaError_t e = cudaSuccess, r;
   const int bytes = int(tc_smem<BN>());
-  if ((r = cudaFuncSetAttribute(gemm_tc_kernel<BN, kEpiStore>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) !=
+  if ((r = set_kernel_smem(gemm_tc_kernel<BN, kEpiStore>, bytes)) !=
       cudaSuccess)
     e = r;
-  if ((r = cudaFuncSetAttribute(gemm_tc_kernel<BN, kEpiResid>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) !=
+  if ((r = set_kernel_smem(gemm_tc_kernel<BN, kEpiResid>, bytes)) !=
       cudaSuccess)
     e = r;
-  if ((r = cudaFuncSetAttribute(gemm_tc_kernel<BN, kEpiSwiglu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                bytes)) != cudaSuccess)
+  if ((r = set_kernel_smem(gemm_tc_kernel<BN, kEpiSwiglu>, bytes)) != cudaSuccess)
     e = r;
-  if ((r = cudaFuncSetAttribute(gemm_tc_kernel<BN, kEpiArgmax>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                bytes)) != cudaSuccess)
+  if ((r = set_kernel_smem(gemm_tc_kernel<BN, kEpiArgmax>, bytes)) != cudaSuccess)
     e = r;
   return e;
 }
@@ -565,6 +563,7 @@ int tc_counter_words(int N, int B) { return (B + 15) / 16 + 2; }
 cudaError_t gemm_tc_init_attributes() {
   cudaError_t e1 = attrs_bn<32>(), e2 = attrs_bn<64>(), e3 = attrs_bn<128>(), e4 = attrs_bn<256>();
   cudaError_t e5 = attrs_bn<16>();
+  if (e5 == cudaSuccess) e5 = set_kernel_smem(embed_rows_kernel, 0);
   return e1 != cudaSuccess ? e1 : e2 != cudaSuccess ? e2 : e3 != cudaSuccess ? e3 : e4 != cudaSuccess ? e4 : e5;
 }
 

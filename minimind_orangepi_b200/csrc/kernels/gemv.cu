@@ -85,31 +85,42 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(ProjArgs a, int rows_per
   pdl_launch_dependents();
 
   // ---------------------------------------------------------------- prologue
+  // All rows' loads are issued before any is used (one L2 round trip for the
+  // whole batch instead of one per row).
   const int B = a.B;
+  const float* srcs[NB];
+#pragma unroll
   for (int b = 0; b < NB; ++b) {
-    float* xb = x_s + b * K;
-    if (b >= B) {
-      for (int k = tid; k < K; k += kThreads) xb[k] = 0.f;
-      continue;
-    }
-    const float* src = a.in + size_t(b) * K;
-    if (PRO == kProEmbedNorm) {
+    srcs[b] = a.in + size_t(b) * K;
+    if (PRO == kProEmbedNorm && b < B) {
       int tok = a.tokens[b];
       if (tok < 0 || tok >= a.vocab) {
         set_error(a.err, kDevBadToken);
         tok = 0;
       }
-      src = a.embed + size_t(tok) * K;
+      srcs[b] = a.embed + size_t(tok) * K;
     }
-    float ss = 0.f;
-    for (int k = tid * 4; k < K; k += kThreads * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(src + k);
-      *reinterpret_cast<float4*>(xb + k) = v;
-      if (PRO == kProEmbedNorm && blockIdx.x == 0) *reinterpret_cast<float4*>(a.hidden + size_t(b) * K + k) = v;
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  float ssb[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) ssb[b] = 0.f;
+  for (int k = tid * 4; k < K; k += kThreads * 4) {
+    float4 v[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      v[b] = b < B ? *reinterpret_cast<const float4*>(srcs[b] + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      *reinterpret_cast<float4*>(x_s + b * K + k) = v[b];
+      if (PRO == kProEmbedNorm && blockIdx.x == 0 && b < B)
+        *reinterpret_cast<float4*>(a.hidden + size_t(b) * K + k) = v[b];
+      ssb[b] += v[b].x * v[b].x + v[b].y * v[b].y + v[b].z * v[b].z + v[b].w * v[b].w;
     }
-    if (PRO != kProPlain) {
-      ss = warp_sum(ss);
+  }
+  if (PRO != kProPlain) {
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      const float ss = warp_sum(ssb[b]);
       if (lane == 0) red[warp][0][b] = ss;
     }
   }
@@ -200,6 +211,24 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(ProjArgs a, int rows_per
   auto epilogue = [&](int r0, int r1, const float* acc0, const float* acc1) {
     const bool has1 = r1 < rows;
     const int g0 = row0 + r0, g1 = row0 + r1;
+    if (EPI == kEpiResid) {
+      // residual add: every row's loads first (one round trip), then the stores
+      bool upd[NB];
+      float o0[NB], o1[NB];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        upd[b] = b < B && (a.row_sel == nullptr || a.row_sel[b] == a.row_sel_val);  // MoE: rows routed here
+        o0[b] = upd[b] ? a.out[size_t(b) * a.ldo + g0] : 0.f;
+        o1[b] = upd[b] && has1 ? a.out[size_t(b) * a.ldo + g1] : 0.f;
+      }
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (!upd[b]) continue;
+        a.out[size_t(b) * a.ldo + g0] = o0[b] + acc0[b];
+        if (has1) a.out[size_t(b) * a.ldo + g1] = o1[b] + acc1[b];
+      }
+      return;
+    }
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       if (b >= B) break;
@@ -207,10 +236,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(ProjArgs a, int rows_per
         a.out[size_t(b) * a.ldo + g0] = acc0[b];
         if (has1) a.out[size_t(b) * a.ldo + g1] = acc1[b];
       } else if (EPI == kEpiResid) {
-        if (a.row_sel == nullptr || a.row_sel[b] == a.row_sel_val) {  // MoE: rows routed to this expert
-          a.out[size_t(b) * a.ldo + g0] += acc0[b];
-          if (has1) a.out[size_t(b) * a.ldo + g1] += acc1[b];
-        }
+        // the read-modify-writes of all rows are done in one pass above
       } else if (EPI == kEpiSwiglu) {
         const float g = acc0[b];
         const int i = (g0 >> 4) * 8 + (g0 & 7);
@@ -313,7 +339,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(ProjArgs a, int rows_per
 
 template <int NB, int PRO, int EPI>
 cudaError_t set_attr() {
-  return cudaFuncSetAttribute(gemv_kernel<NB, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  return set_kernel_smem(gemv_kernel<NB, PRO, EPI>, 200 * 1024);
 }
 
 template <int NB>

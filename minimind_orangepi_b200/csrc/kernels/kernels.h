@@ -114,6 +114,43 @@ struct TcArgs {
   const int* row_sel = nullptr;  // kEpiResid: update only rows b with row_sel[b] == row_sel_val (MoE)
   int row_sel_val = 0;
 };
+// Small-batch projection (5..64 rows) on mma.sync (skinny.cu): weights in
+// the skinny fragment order (launch_pack_skinny), each CTA owning T 16-row
+// tiles over the full K; inputs, outputs and the folded RMSNorm as TcArgs,
+// except that sums of squares are per CTA: a consumer reads ss_parts partials
+// per row (ss_in[b * ss_parts + m]); a kEpiResid producer writes
+// skinny_grid(N) of them (ss_out[b * grid + blockIdx.x]).
+constexpr int kSkinnyMaxBatch = 64;
+constexpr int kSkinnyMaxSmem = 200 * 1024;
+struct SkinnyArgs {
+  const __half* Wf = nullptr;  // [N / 16 tiles][K / 32 blocks][2 steps][32 lanes][8 halves]
+  const __half* X = nullptr;   // [B][K] fp16
+  int N = 0, K = 0, B = 0;
+  int T = 1;  // tiles per CTA (set by the launcher)
+  float* out = nullptr;     // kEpiStore / kEpiResid: [B][ldo] fp32
+  __half* out16 = nullptr;  // kEpiSwiglu: [B][ldo] fp16
+  int ldo = 0;
+  const float* ss_in = nullptr;
+  int ss_parts = 0;
+  float eps = 0.f;
+  __half* h16_out = nullptr;  // kEpiResid: [B][N] fp16 copy of the updated rows
+  float* ss_out = nullptr;
+  const int* row_sel = nullptr;
+  int row_sel_val = 0;
+  float* logits = nullptr;       // kEpiArgmax: optional [B][N]
+  void* argmax_part = nullptr;   // kEpiArgmax: [B][grid] (value, index)
+  unsigned* counter = nullptr;   // kEpiArgmax: one zeroed, self-resetting word
+  TokenSink sink;
+  int* err = nullptr;
+};
+int skinny_tiles_per_cta(int N, int num_sms);
+int skinny_grid(int N, int num_sms);
+size_t skinny_smem_bytes(int N, int K, int B, int num_sms);
+bool skinny_supported(int N, int K, int B, int num_sms);
+cudaError_t skinny_init_attributes();
+cudaError_t launch_skinny(int epi, const SkinnyArgs& a, int num_sms, cudaStream_t stream, bool pdl);
+cudaError_t launch_pack_skinny(const __half* src, __half* dst, int64_t N, int64_t K, cudaStream_t s);
+
 int tc_batch_tile(int N, int B);
 // split-K factor the launcher uses for this projection (1 = none)
 // (environment overrides MMC_TC_SPLIT, MMC_TC_SPLIT_BN, MMC_TC_SPLIT_TARGET)

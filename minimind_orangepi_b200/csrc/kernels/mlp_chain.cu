@@ -355,8 +355,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) mlp_chain_kernel(const __gri
 int chain_sync_words(int B) { return 2 + 2 * ((B + CBN - 1) / CBN); }
 
 cudaError_t mlp_chain_init_attributes() {
-  return cudaFuncSetAttribute(mlp_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kChainStages * ST_BYTES + 1024);
+  return set_kernel_smem(mlp_chain_kernel, kChainStages * ST_BYTES + 1024);
 }
 
 cudaError_t launch_mlp_chain(const ChainArgs& a_in, int max_ctas, cudaStream_t s, bool pdl) {

@@ -1062,7 +1062,7 @@ __global__ void pack_fragments_kernel(const __half* __restrict__ src, __half* __
 
 template <int HD>
 cudaError_t attr_step() {
-  return cudaFuncSetAttribute(step_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+  return set_kernel_smem(step_kernel<HD>, int(kSmemBytes));
 }
 
 template <int HD>

@@ -89,6 +89,8 @@ struct Layer {
   std::vector<__half*> egu, edown;          // MoE: per expert [2 MI][H] (interleaved, folded), [H][MI]
   // the same dense projections in fragment order for the persistent step
   __half *qkv_f = nullptr, *o_f = nullptr, *gu_f = nullptr, *down_f = nullptr;
+  // the same in the small-batch (skinny.cu) fragment order
+  __half *qkv_s = nullptr, *o_s = nullptr, *gu_s = nullptr, *down_s = nullptr;
 };
 
 }  // namespace
@@ -155,6 +157,10 @@ struct mmc_ctx {
   float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
   // persistent step (batches of up to kStepMaxRows rows, dense models)
   bool persistent = false;  // MMC_PERSISTENT at creation (default off: measured slower than the chain)
+  bool skinny = true;       // MMC_SKINNY at creation: 5..64-row batches on the skinny.cu projections
+  __half* lm_s = nullptr;   // lm_head in the skinny fragment order
+  int ss_cap = 0;           // sums-of-squares slots per row (the larger of the two paths' producers)
+  int part_cap = 0;         // argmax partial slots per row
   __half* lm_f = nullptr;
   float* step_ssp = nullptr;       // [rows][H / 16]
   float* step_part = nullptr;      // [rows][nkv][max_pages][rep][hd + 2]
@@ -326,6 +332,19 @@ int chain_ctas(const mmc_ctx* c) {
   return v > 0 ? v : c->num_sms;
 }
 
+// Batches of 5..kSkinnyMaxBatch rows of a dense model run their projections on
+// skinny.cu when the context packed its weights for it and every projection
+// fits the kernel at this batch size.
+bool use_skinny(const mmc_ctx* c, int B) {
+  if (c->lm_s == nullptr || B <= kGemvMaxBatch || B > mmc::kSkinnyMaxBatch || use_mlp_chain(c) || c->moe_experts > 0)
+    return false;
+  const auto& d = c->d;
+  const int H = int(d.hidden_size), I = int(d.intermediate_size), Q = int(c->q_size());
+  const int NQKV = Q + 2 * int(c->kv_size()), V = int(d.vocab_size);
+  auto ok = [&](int N, int K) { return mmc::skinny_supported(N, K, B, c->num_sms); };
+  return ok(NQKV, H) && ok(H, Q) && ok(2 * I, H) && ok(H, I) && ok(V, H);
+}
+
 void launch_proj(mmc_ctx* c, int pro, int epi, const mmc::ProjArgs& a, cudaStream_t s, bool pdl) {
   ck(mmc::launch_gemv(pro, epi, a, c->num_sms, s, pdl), "projection launch");
 }
@@ -351,10 +370,11 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   float* const attn_part = c->attn_part + r0 * size_t(d.num_key_value_heads) * c->max_splits_cap * c->rep() *
                                                 size_t(d.head_dim + 2);
   unsigned* const attn_counters = c->attn_counters + r0 * size_t(d.num_key_value_heads);
-  void* const argmax_part = static_cast<uint8_t*>(c->argmax_part) + r0 * size_t((d.vocab_size + 127) / 128) * 8;
+  void* const argmax_part = static_cast<uint8_t*>(c->argmax_part) + r0 * size_t(c->part_cap) * 8;
   unsigned* const argmax_counter = c->argmax_counter + size_t(io.part) * size_t(c->max_batch + 2);
   int* const expert_ids = c->expert_ids + r0;  // MoE: routed expert per row
   const bool tc = io.B > kGemvMaxBatch;
+  const bool sk = tc && use_skinny(c, io.B);
   int evi = 0;
   bool first = true;
   // returns whether this launch may use programmatic overlap
@@ -368,7 +388,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   // tensor-core path: h16 holds the fp16 residual rows, ss their per-M-tile
   // sums of squares; each RMSNorm is the norm weight folded into the next
   // projection's W and a 1/rms scale in its epilogue.
-  float* const ss = c->ss + r0 * size_t((H + 127) / 128);
+  float* const ss = c->ss + r0 * size_t(c->ss_cap);
   auto embed_rows = [&] {
     mmc::EmbedArgs e;
     e.embed = c->embed;
@@ -382,6 +402,34 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     e.err = c->err;
     const bool pdl = mark(kKindNorm);
     ck(mmc::launch_embed_rows(e, s, pdl), "embedding launch");
+  };
+  // sums-of-squares partials per row left by the last producer of the
+  // residual rows (the embedding gather, or a skinny residual projection)
+  int ss_parts = int((H + 127) / 128);
+  auto skproj = [&](Kind k, int epi, const __half* Wf, int N, int K, const __half* X, float* out, __half* out16,
+                    int ldo, bool normed) {
+    mmc::SkinnyArgs t;
+    t.Wf = Wf;
+    t.X = X;
+    t.N = N;
+    t.K = K;
+    t.B = io.B;
+    t.out = out;
+    t.out16 = out16;
+    t.ldo = ldo;
+    if (normed) {
+      t.ss_in = ss;
+      t.ss_parts = ss_parts;
+      t.eps = d.rms_norm_eps;
+    }
+    if (epi == mmc::kEpiResid) {
+      t.h16_out = h16;
+      t.ss_out = ss;
+    }
+    t.err = c->err;
+    const bool pdl = mark(k);
+    ck(mmc::launch_skinny(epi, t, c->num_sms, s, pdl), "skinny projection launch");
+    if (epi == mmc::kEpiResid) ss_parts = mmc::skinny_grid(N, c->num_sms);
   };
   // normed: the input is the residual stream (scale by 1/rms); resid: update
   // the residual stream and emit its fp16 copy and sums of squares
@@ -420,7 +468,10 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   for (int l = 0; l < int(d.num_hidden_layers); ++l) {
     const Layer& L = c->layers[l];
     // ---- q|k|v projection
-    if (tc) {
+    if (sk) {
+      if (l == 0) embed_rows();
+      skproj(kKindQkv, mmc::kEpiStore, L.qkv_s, NQKV, H, h16, qkv, nullptr, NQKV, true);
+    } else if (tc) {
       if (l == 0) embed_rows();
       tcproj(kKindQkv, mmc::kEpiStore, L.qkv, NQKV, H, h16, qkv, nullptr, NQKV, true);
     } else {
@@ -481,6 +532,12 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     {
       const bool pdl = mark(kKindAttn);
       ck(mmc::launch_attention(a, s, pdl), "attention launch");
+    }
+    if (sk) {
+      skproj(kKindO, mmc::kEpiResid, L.o_s, H, Q, attn16, hidden, nullptr, H, false);
+      skproj(kKindGateUp, mmc::kEpiSwiglu, L.gu_s, 2 * I, H, h16, nullptr, act16, I, true);
+      skproj(kKindDown, mmc::kEpiResid, L.down_s, H, I, act16, hidden, nullptr, H, false);
+      continue;
     }
     if (tc) {
       if (c->moe_experts > 0) {
@@ -640,7 +697,24 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   sink.hist_step = io.hist_step;
   sink.hist_cap = io.hist_cap;
   sink.hist_stride = io.hist_stride > 0 ? io.hist_stride : io.B;
-  if (tc) {
+  if (sk) {
+    mmc::SkinnyArgs t;
+    t.Wf = c->lm_s;
+    t.X = h16;
+    t.N = int(d.vocab_size);
+    t.K = H;
+    t.B = io.B;
+    t.ss_in = ss;
+    t.ss_parts = ss_parts;
+    t.eps = d.rms_norm_eps;
+    t.logits = io.logits;
+    t.argmax_part = argmax_part;
+    t.counter = argmax_counter;
+    t.sink = sink;
+    t.err = c->err;
+    const bool pdl = mark(kKindLm);
+    ck(mmc::launch_skinny(mmc::kEpiArgmax, t, c->num_sms, s, pdl), "lm_head launch");
+  } else if (tc) {
     mmc::TcArgs t;
     t.W = c->lm_head;
     t.X = h16;
@@ -987,6 +1061,16 @@ bool step_shape_ok(const mmc_ctx* c) {
          d.hidden_size <= mmc::kStepMaxK && d.intermediate_size <= mmc::kStepMaxK && Q <= mmc::kStepMaxK;
 }
 
+// Whether every dense projection has a skinny.cu form (16-row tiles, 32-column
+// blocks).
+bool skinny_shape_ok(const mmc_ctx* c) {
+  const auto& d = c->d;
+  const int H = int(d.hidden_size), I = int(d.intermediate_size), Q = int(c->q_size());
+  const int NQKV = Q + 2 * int(c->kv_size()), V = int(d.vocab_size);
+  auto ok = [&](int N, int K) { return mmc::skinny_supported(N, K, 1, c->num_sms); };
+  return ok(NQKV, H) && ok(H, Q) && ok(2 * I, H) && ok(H, I) && ok(V, H);
+}
+
 // Every packed weight buffer of a loaded context, in the order of the packed
 // cache file: (device pointer slot, bytes). With allocate, the buffers are
 // allocated first (loading a cache).
@@ -1140,6 +1224,21 @@ void finish_load(mmc_ctx* c) {
     }
     c->lm_f = frag(c->lm_head, d.vocab_size, H);
   }
+  if (c->skinny && c->moe_experts == 0 && skinny_shape_ok(c)) {
+    const int64_t H = d.hidden_size, I = d.intermediate_size, Q = c->q_size(), NQKV = Q + 2 * c->kv_size();
+    auto pack = [&](const __half* src, int64_t N, int64_t K) {
+      __half* dst = c->alloc<__half>(size_t(N * K), "skinny fragment-order weights");
+      ck(mmc::launch_pack_skinny(src, dst, N, K, c->stream), "skinny packing");
+      return dst;
+    };
+    for (auto& L : c->layers) {
+      L.qkv_s = pack(L.qkv, NQKV, H);
+      L.o_s = pack(L.o, H, Q);
+      L.gu_s = pack(L.gu, 2 * I, H);
+      L.down_s = pack(L.down, H, I);
+    }
+    c->lm_s = pack(c->lm_head, d.vocab_size, H);
+  }
   const auto cos_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, false);
   const auto sin_t = rope_table(d.max_position_embeddings, d.head_dim, d.rope_theta, true);
   c->rope_cos = c->alloc<float>(cos_t.size(), "rope");
@@ -1211,9 +1310,11 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     c->mlp_chain = env_int("MMC_MLP_CHAIN", 0) != 0;
     c->persistent = env_int("MMC_PERSISTENT", 0) != 0;
     c->attn_fused = env_int("MMC_ATTN_FUSED", 1) != 0;
+    c->skinny = env_int("MMC_SKINNY", 1) != 0;
     c->step_trace_on = env_int("MMC_STEP_TRACE", 0) != 0;
     ck(mmc::step_init_attributes(), "persistent step attributes");
     ck(mmc::gemv_init_attributes(), "gemv attributes");
+    ck(mmc::skinny_init_attributes(), "skinny projection attributes");
     ck(mmc::gemm_tc_init_attributes(), "tensor-core projection attributes");
     ck(mmc::mlp_chain_init_attributes(), "projection chain attributes");
     ck(mmc::attention_init_attributes(), "attention attributes");
@@ -1421,6 +1522,8 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     for (int b = 1; b <= std::min(max_batch, 4); ++b)
       part_bytes = std::max(part_bytes, mmc::gemv_argmax_part_bytes(V, H, b, c->num_sms));
     part_bytes = std::max(part_bytes, mmc::tc_argmax_part_bytes(V, max_batch));
+    c->part_cap = int(std::max<int64_t>((V + 127) / 128, mmc::skinny_grid(int(V), c->num_sms)));
+    part_bytes = std::max(part_bytes, size_t(max_batch) * c->part_cap * 8);
     c->argmax_part = c->alloc<uint8_t>(part_bytes, "argmax partials");
     c->argmax_counter = c->alloc<unsigned>(kMaxParts * (size_t(max_batch) + 2), "argmax counters (per batch part)");
     c->attn_part = c->alloc<float>(
@@ -1430,7 +1533,8 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
     c->attn_work = c->alloc<unsigned>(4 * kMaxParts, "attention work queues (per batch part)");
     c->chain_words = mmc::chain_sync_words(max_batch);
     c->chain_sync = c->alloc<unsigned>(size_t(kMaxParts) * c->chain_words, "projection-chain queues (per batch part)");
-    c->ss = c->alloc<float>(size_t(max_batch) * ((H + 127) / 128), "residual sums of squares");
+    c->ss_cap = int(std::max<int64_t>((H + 127) / 128, mmc::skinny_grid(int(H), c->num_sms)));
+    c->ss = c->alloc<float>(size_t(max_batch) * c->ss_cap, "residual sums of squares");
     if (c->lm_f != nullptr) {  // persistent step scratch (its batches have at most kStepMaxRows rows)
       const size_t rows = size_t(std::min(max_batch, kStepMaxRows));
       c->step_ssp = c->alloc<float>(rows * (H / 16), "step sums of squares");

@@ -109,7 +109,8 @@ def test_decode_matches_live_oracle(shape, plen, steps, model_dir):
 
 @pytest.mark.parametrize("shape,batch,steps", [("tiny-moe", 3, 20), ("tiny-moe", 37, 16), ("tiny-moe", 260, 4),
                                               ("tiny-hd64", 3, 30), ("tiny-hd64", 37, 24),
-                                               ("minimind2-small", 8, 12), ("tiny-hd96", 70, 12)])
+                                               ("minimind2-small", 8, 12), ("tiny-hd96", 70, 12),
+                                               ("minimind2", 20, 4)])
 def test_batched_decode_matches_oracle(shape, batch, steps, model_dir):
     """Independent sequences with different prompt lengths decode together;
     each row must match its own single-sequence reference run."""
