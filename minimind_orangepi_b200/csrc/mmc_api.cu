@@ -246,7 +246,13 @@ void check_device_error(mmc_ctx* c) {
 }
 
 // Split size for the attention kernel: enough CTAs to cover the SMs a few
-// times over, at most `max_splits_cap` splits per sequence.
+// times over, at most `max_splits_cap` splits per sequence, and at least
+// kMinSplitPages pages per split. (Measured on B200, MiniMind2, 1..128 rows x
+// 200..3000 positions, forcing every split size from 2 to 48 pages: this rule
+// is within 3 % of the best size on average; one-page splits, the previous
+// rule at small batches, spent more on their merges than the extra CTAs
+// gained: 32 rows at 1100 positions 657 -> 559 us per step.)
+constexpr int64_t kMinSplitPages = 8;
 int plan_split_raw(int64_t total_pages, int64_t nkv, int num_sms, int cap, int64_t max_ctx, int* max_splits) {
   const int64_t pages = std::max<int64_t>(1, (max_ctx + mmc::kPageTokens - 1) / mmc::kPageTokens);
   // work items per persistent attention CTA (2 per SM): enough that the
@@ -257,6 +263,7 @@ int plan_split_raw(int64_t total_pages, int64_t nkv, int num_sms, int cap, int64
     return v > 0 ? v : 1;
   }();
   int64_t sp = std::max<int64_t>(1, total_pages * nkv / (int64_t(items_per_cta) * 2 * num_sms));
+  sp = std::max<int64_t>(sp, std::min<int64_t>(kMinSplitPages, pages));
   sp = std::max<int64_t>(sp, (pages + cap - 1) / cap);
   sp = std::min<int64_t>(sp, pages);
   *max_splits = int((pages + sp - 1) / sp);
