@@ -57,8 +57,15 @@ __device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uin
                : "memory");
 }
 
+// Input rows larger than kXWhole bytes are staged in chunks of at most
+// kXChunk bytes through two buffers (the next chunk's copies in flight while
+// the warps multiply the current one).
+constexpr int kXWhole = 128 * 1024;
+constexpr int kXChunk = 64 * 1024;
+
 struct SkLayout {
   size_t w_bytes, x_bytes, red_bytes, stash_bytes, total;
+  int cb;  // 32-column blocks per input chunk (nb when staged whole)
 };
 // rows of the cross-warp partial tiles are padded by 8 floats so that the
 // float2 stores of one warp hit distinct banks
@@ -67,7 +74,9 @@ __host__ __device__ inline SkLayout sk_layout(int T, int K, int NT) {
   SkLayout s;
   const int nb = K / 32;
   s.w_bytes = size_t(T) * nb * 1024;
-  s.x_bytes = size_t(NT) * nb * 512;
+  const int per_block = NT * 512;
+  s.cb = nb * per_block <= kXWhole ? nb : kXChunk / per_block;
+  s.x_bytes = size_t(s.cb < nb ? 2 : 1) * s.cb * per_block;
   s.red_bytes = size_t(kWarps) * 16 * red_ld(NT) * 4;
   s.stash_bytes = size_t(NT) * 8 * T * 16 * 4;
   // red aliases the input stage, the epilogue stash the weight slab (both
@@ -114,14 +123,21 @@ __global__ void __launch_bounds__(kThreads, 2) skinny_kernel(const SkinnyArgs a)
   pdl_wait();
   pdl_launch_dependents();
 
-  // ---- input rows: [block][n-tile][lane] 16-byte pieces, zero past row B
-  const int pieces = NT * nb * 32;
-  for (int i = tid; i < pieces; i += kThreads) {
-    const int ln = i & 31, j = (i >> 5) % NT, blk = (i >> 5) / NT;
-    const int row = 8 * j + (ln >> 2);
-    const __half* src = a.X + size_t(row < B ? row : 0) * K + blk * 32 + 8 * (ln & 3);
-    cp_async16_zfill(x_s + size_t(i) * 16, src, row < B ? 16u : 0u);
-  }
+  // ---- input rows: [block][n-tile][lane] 16-byte pieces, zero past row B,
+  //      chunk c (blocks [c * cb, c * cb + cb)) into buffer c & 1
+  const int cb = L.cb, nchunks = (nb + cb - 1) / cb;
+  const size_t xbuf = size_t(cb) * NT * 512;
+  auto stage = [&](int c) {
+    const int blk0 = c * cb, nblk = min(cb, nb - blk0);
+    uint8_t* dst = x_s + (c & 1) * xbuf;
+    for (int i = tid; i < NT * nblk * 32; i += kThreads) {
+      const int ln = i & 31, j = (i >> 5) % NT, blk = blk0 + (i >> 5) / NT;
+      const int row = 8 * j + (ln >> 2);
+      const __half* src = a.X + size_t(row < B ? row : 0) * K + blk * 32 + 8 * (ln & 3);
+      cp_async16_zfill(dst + size_t(i) * 16, src, row < B ? 16u : 0u);
+    }
+  };
+  stage(0);
   cp_async_commit();
   // ---- folded RMSNorm: 1/rms per batch row from the producer's partial
   //      sums (warp w takes rows w, w + 8, ...; every load is issued before
@@ -148,30 +164,40 @@ __global__ void __launch_bounds__(kThreads, 2) skinny_kernel(const SkinnyArgs a)
     }
   }
   if (!mbar_wait_bounded(&wbar, 0, a.err)) abort_flag = 1;
-  cp_async_wait<0>();
-  __syncthreads();
 
-  // ---- warp w: tile w % T, K-range part w / T
+  // ---- warp w: tile w % T, K-range part w / T of every chunk
   const int kparts = kWarps / T;
   const int tw = warp % T, kp = warp / T;
   float acc[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-  if (!abort_flag && tw < my_tiles) {
-    const int b0 = kp * nb / kparts, b1 = (kp + 1) * nb / kparts;
-    const uint8_t* wt = w_s + size_t(tw) * nb * 1024 + lane * 16;
-    const uint8_t* xt = x_s + lane * 16;
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) {
+      stage(c + 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (!abort_flag && tw < my_tiles) {
+      const int blk0 = c * cb, nblk = min(cb, nb - blk0);
+      const int b0 = kp * nblk / kparts, b1 = (kp + 1) * nblk / kparts;
+      const uint8_t* wt = w_s + size_t(tw) * nb * 1024 + size_t(blk0) * 1024 + lane * 16;
+      const uint8_t* xt = x_s + (c & 1) * xbuf + lane * 16;
 #pragma unroll 2
-    for (int blk = b0; blk < b1; ++blk) {
-      const uint4 w0 = *reinterpret_cast<const uint4*>(wt + size_t(blk) * 1024);
-      const uint4 w1 = *reinterpret_cast<const uint4*>(wt + size_t(blk) * 1024 + 512);
+      for (int blk = b0; blk < b1; ++blk) {
+        const uint4 w0 = *reinterpret_cast<const uint4*>(wt + size_t(blk) * 1024);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(wt + size_t(blk) * 1024 + 512);
 #pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const uint4 x = *reinterpret_cast<const uint4*>(xt + (size_t(blk) * NT + j) * 512);
-        mma16816(acc[j], w0.x, w0.y, w0.z, w0.w, x.x, x.y);
-        mma16816(acc[j], w1.x, w1.y, w1.z, w1.w, x.z, x.w);
+        for (int j = 0; j < NT; ++j) {
+          const uint4 x = *reinterpret_cast<const uint4*>(xt + (size_t(blk) * NT + j) * 512);
+          mma16816(acc[j], w0.x, w0.y, w0.z, w0.w, x.x, x.y);
+          mma16816(acc[j], w1.x, w1.y, w1.z, w1.w, x.z, x.w);
+        }
       }
     }
+    if (c + 1 < nchunks) __syncthreads();  // buffer c & 1 is restaged two chunks later
   }
   __syncthreads();  // every warp is done with the input stage and the weight slab
   constexpr int ld = red_ld(NT);
