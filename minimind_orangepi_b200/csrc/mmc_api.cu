@@ -157,7 +157,8 @@ struct mmc_ctx {
   float* ss = nullptr;  // [max_batch][ceil(H / 128)] residual-row sums of squares (folded RMSNorm)
   // persistent step (batches of up to kStepMaxRows rows, dense models)
   bool persistent = false;  // MMC_PERSISTENT at creation (default off: measured slower than the chain)
-  bool skinny = true;       // MMC_SKINNY at creation: 5..64-row batches on the skinny.cu projections
+  bool skinny = true;       // MMC_SKINNY at creation: small batches on the skinny.cu projections
+  int skinny_min_rows = env_int("MMC_SKINNY_MIN_ROWS", 2);  // smallest batch on them (1 row: gemv measured faster)
   __half* lm_s = nullptr;   // lm_head in the skinny fragment order
   int ss_cap = 0;           // sums-of-squares slots per row (the larger of the two paths' producers)
   int part_cap = 0;         // argmax partial slots per row
@@ -300,6 +301,10 @@ struct StepIO {
 // fused RMSNorm prologues; larger batches the tensor-core projections with the
 // RMSNorms folded across kernels. Both run 6 kernels per layer.
 constexpr int kGemvMaxBatch = 4;
+bool use_skinny(const mmc_ctx* c, int B);
+// the CUDA-core projections serve batches of up to kGemvMaxBatch rows that
+// the skinny projections do not take
+bool use_gemv(const mmc_ctx* c, int B) { return B <= kGemvMaxBatch && !use_skinny(c, B); }
 enum Kind { kKindQkv = 0, kKindAttn = 1, kKindO = 2, kKindGateUp = 3, kKindDown = 4, kKindLm = 5, kKindNorm = 6 };
 
 // With MMC_MLP_CHAIN=1 (read when a context is created) the tensor-core path
@@ -318,18 +323,18 @@ int kernels_per_step(const mmc_ctx* c, int B, bool alone = true) {
   if (c->attn_fused && alone) {  // attention is one launch (q/k prep fused in)
     if (c->moe_experts > 0) {
       const int per = 4 + 2 * c->moe_experts;
-      return B <= kGemvMaxBatch ? per * L + 1 : per * L + 2;
+      return use_gemv(c, B) ? per * L + 1 : per * L + 2;
     }
-    if (B <= kGemvMaxBatch) return 5 * L + 1;
+    if (use_gemv(c, B)) return 5 * L + 1;
     return (use_mlp_chain(c) ? 3 : 5) * L + 2;
   }
   // attention is two launches; the tensor-core path adds the layer-0
   // embedding gather (its RMSNorms are folded into the projections)
   if (c->moe_experts > 0) {  // o, router and gate/up + down per expert replace the dense MLP
     const int per = 5 + 2 * c->moe_experts;
-    return B <= kGemvMaxBatch ? per * L + 1 : per * L + 2;
+    return use_gemv(c, B) ? per * L + 1 : per * L + 2;
   }
-  if (B <= kGemvMaxBatch) return 6 * L + 1;
+  if (use_gemv(c, B)) return 6 * L + 1;
   return (use_mlp_chain(c) ? 4 : 6) * L + 2;
 }
 
@@ -343,7 +348,8 @@ int chain_ctas(const mmc_ctx* c) {
 // skinny.cu when the context packed its weights for it and every projection
 // fits the kernel at this batch size.
 bool use_skinny(const mmc_ctx* c, int B) {
-  if (c->lm_s == nullptr || B <= kGemvMaxBatch || B > mmc::kSkinnyMaxBatch || use_mlp_chain(c) || c->moe_experts > 0)
+  if (c->lm_s == nullptr || B < c->skinny_min_rows || B > mmc::kSkinnyMaxBatch || use_mlp_chain(c) ||
+      c->moe_experts > 0)
     return false;
   const auto& d = c->d;
   const int H = int(d.hidden_size), I = int(d.intermediate_size), Q = int(c->q_size());
@@ -380,8 +386,8 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   void* const argmax_part = static_cast<uint8_t*>(c->argmax_part) + r0 * size_t(c->part_cap) * 8;
   unsigned* const argmax_counter = c->argmax_counter + size_t(io.part) * size_t(c->max_batch + 2);
   int* const expert_ids = c->expert_ids + r0;  // MoE: routed expert per row
-  const bool tc = io.B > kGemvMaxBatch;
-  const bool sk = tc && use_skinny(c, io.B);
+  const bool sk = use_skinny(c, io.B);
+  const bool tc = !use_gemv(c, io.B);
   int evi = 0;
   bool first = true;
   // returns whether this launch may use programmatic overlap
@@ -2118,7 +2124,7 @@ int mmc_kernels_per_step(const mmc_ctx* c, int32_t batch, int32_t* k) {
       return;
     }
     // a batch that runs as concurrent parts launches each part's chain
-    const int P = batch > kGemvMaxBatch ? batch_parts(c, batch) : 1;
+    const int P = use_gemv(c, batch) ? 1 : batch_parts(c, batch);
     int total = 0;
     for (int i = 0; i < P; ++i) {
       int r0 = 0, n = batch;

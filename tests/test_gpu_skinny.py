@@ -1,4 +1,4 @@
-"""Projections of 5..64-row decode batches on the skinny mma.sync kernel
+"""Projections of 2..64-row decode batches on the skinny mma.sync kernel
 (skinny.cu, the default) against the tcgen05 projections (a context created
 with MMC_SKINNY=0) on the same prompts. The two paths sum each dot product in
 a different order, so logits agree to the decode tolerance, not bitwise:
@@ -34,7 +34,7 @@ def engine(d, skinny: bool, n):
 
 @pytest.mark.parametrize("shape_name,n,plen", [("minimind2", 64, 900), ("minimind2", 41, 300),
                                                ("minimind2", 32, 1100), ("minimind2", 17, 300),
-                                               ("minimind2-small", 8, 600), ("tiny-hd64", 5, 200),
+                                               ("minimind2-small", 8, 600), ("tiny-hd64", 5, 200), ("minimind2-small", 3, 400), ("tiny-hd64", 2, 100),
                                                ("tiny-hd96", 24, 150)])
 def test_skinny_matches_tensor_core_path(shape_name, n, plen):
     shape = SHAPES[shape_name]
