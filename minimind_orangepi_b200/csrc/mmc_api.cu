@@ -386,7 +386,11 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
   void* const argmax_part = static_cast<uint8_t*>(c->argmax_part) + r0 * size_t(c->part_cap) * 8;
   unsigned* const argmax_counter = c->argmax_counter + size_t(io.part) * size_t(c->max_batch + 2);
   int* const expert_ids = c->expert_ids + r0;  // MoE: routed expert per row
-  const bool sk = use_skinny(c, io.B);
+  // concurrent batch parts keep the tcgen05 projections: skinny CTAs of 64
+  // rows hold up to 192 KB of shared memory, which the parts' kernels then
+  // cannot share an SM with (config 4, 256 rows as 4 parts x 64: 1.93 vs
+  // 1.49 ms per step measured on B200)
+  const bool sk = io.alone && use_skinny(c, io.B);
   const bool tc = !use_gemv(c, io.B);
   int evi = 0;
   bool first = true;
