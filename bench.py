@@ -290,7 +290,7 @@ def main() -> None:
     lens, prompts = workload_prompts(w)
     K, W = args.steps, args.warmup
     E = K  # end-to-end steps through the host-buffer C ABI
-    need = [n + W + K + E + K + 2 for n in lens]  # + K streamed steps
+    need = [n + W + K + E + 2 * K + 2 for n in lens]  # + K graph steps and K streamed steps
     shards = plan_shards(need, world)
     mine = shards[rank]
     B = len(mine)
@@ -354,8 +354,15 @@ def main() -> None:
         toks, _ = eng.step(seqs, toks)
     e2e_s = time.perf_counter() - t0
     # ---------------- streamed: the device loop with each step's tokens read on the host as it lands
-    # (mmc_graph_stream_*: what generate_stream and --stream use), host wall clock
+    # (mmc_graph_stream_*: what generate_stream and --stream use), host wall clock; beside it, K plain
+    # graph replays right before it (device events), so that both see nearly the same context lengths
     eng.graph_set_tokens(toks)
+    ev0.record(stream)
+    eng.graph_run(K, sptr)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    graph_near_ms = ev0.elapsed_time(ev1)
+    eng.graph_set_tokens(eng.graph_tokens(K)[-1].copy())
     t0 = time.perf_counter()
     for _ in eng.graph_stream(K):
         pass
@@ -438,6 +445,7 @@ def main() -> None:
                 "prompt_pass": "synthetic K/V fast-forward" if args.fill_context else "device prompt pass (mmc_prefill)",
             },
             "stream": {"value": w["n_seqs"] * K / stream_s, "unit": "tokens/s",
+                       "graph_replay_before": w["n_seqs"] * K / (graph_near_ms / 1000.0),
                        "path": "graph replays whose lm_head epilogue writes each step's tokens to mapped pinned host memory, read by the host "
                                "as they land (host wall clock, rank 0)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 8 * w["n_seqs"],

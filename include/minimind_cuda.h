@@ -237,10 +237,12 @@ MMC_EXPORT int mmc_synchronize(mmc_ctx* ctx);
 /* Number of kernels one decode step launches for a batch of `batch` rows:
  * 1 for batches of up to 64 rows on dense models when the context was
  * created with MMC_PERSISTENT=1 (the persistent step: the whole step is one
- * cooperative launch); otherwise 5 per layer + 1 for
- * batch <= 4, and above, 5 per layer + 2 for each of the concurrent parts the
- * batch runs as (up to 4 parts of >= 64 rows); one more per layer when the
- * context was created with MMC_ATTN_FUSED=0 (separate q/k prep launch). */
+ * cooperative launch); otherwise 5 per layer + 1 for batch 1 (and for 2..4
+ * rows when the model's shapes do not fit the small-batch projections), 5 per
+ * layer + 2 for a larger batch that runs as one part (below 256 rows), and
+ * 6 per layer + 2 for each of the concurrent parts of a batch of 256+ rows (up
+ * to 4 parts of >= 64 rows; the parts keep the separate q/k prep launch); one
+ * more per layer when the context was created with MMC_ATTN_FUSED=0. */
 MMC_EXPORT int mmc_kernels_per_step(const mmc_ctx* ctx, int32_t batch, int32_t* kernels);
 
 /* ------------------------------------------------------------- single ops
