@@ -175,7 +175,8 @@ struct mmc_ctx {
   int* err = nullptr;
   int* h_stage = nullptr;  // pinned: [2][max_batch] ints
   int max_splits_cap = 64;
-  std::vector<int> async_slots;  // slot list currently in `slots` for mmc_decode_step_async
+  std::vector<int> async_slots;  // slot list currently in `slots` (empty: unknown); uploads are skipped when equal
+  int64_t hist_host = 0;         // host copy of the history counter: replays since its last reset
 
   // graph loop
   cudaGraphExec_t graph = nullptr;
@@ -1721,16 +1722,20 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
     for (int b = 0; b < batch; ++b)
       require(tokens[b] >= 0 && tokens[b] < c->d.vocab_size, MMC_ERR_OUT_OF_RANGE,
               "token id out of vocabulary range");
-    std::memcpy(c->h_stage, seq_ids, sizeof(int) * batch);
-    std::memcpy(c->h_stage + batch, tokens, sizeof(int) * batch);
-    ck(cudaMemcpyAsync(c->slots, c->h_stage, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream), "H2D slots");
-    c->async_slots.clear();
-    ck(cudaMemcpyAsync(c->tokens, c->h_stage + batch, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream),
-       "H2D tokens");
     const bool use_graph = c->graph && !logits_host && batch == c->graph_batch &&
                            std::equal(seq_ids, seq_ids + batch, c->graph_slots.begin()) &&
                            std::all_of(seq_ids, seq_ids + batch,
                                        [&](int32_t q) { return c->h_pos[q] + 1 <= c->graph_cap_tokens; });
+    // host staging: [slots][tokens][error word]; the slot list is uploaded only
+    // when `slots` holds another one
+    std::memcpy(c->h_stage + batch, tokens, sizeof(int) * batch);
+    if (c->async_slots.size() != size_t(batch) || !std::equal(seq_ids, seq_ids + batch, c->async_slots.begin())) {
+      std::memcpy(c->h_stage, seq_ids, sizeof(int) * batch);
+      ck(cudaMemcpyAsync(c->slots, c->h_stage, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream), "H2D slots");
+      c->async_slots.assign(seq_ids, seq_ids + batch);
+    }
+    ck(cudaMemcpyAsync(c->tokens, c->h_stage + batch, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream),
+       "H2D tokens");
     io.slots = c->slots;
     io.tokens = c->tokens;
     io.logits = logits_host ? c->logits : nullptr;
@@ -1740,14 +1745,19 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
          "H2D attention order");
       io.order = c->attn_order;
     }
+    // a graph replay's argmax epilogue writes the next tokens into the mapped
+    // history as well: only the device error word is copied back
+    const int* next_host = c->h_stage + 2 * batch;
     if (use_graph) {
       ck(cudaGraphLaunch(c->graph, c->stream), "graph launch");
+      next_host = c->h_hist + size_t(c->hist_host % c->hist_cap) * c->graph_batch;
+      ++c->hist_host;
     } else {
       enqueue_batch(c, io, c->stream);
+      ck(cudaMemcpyAsync(c->h_stage + 2 * batch, c->tokens, sizeof(int) * batch, cudaMemcpyDeviceToHost, c->stream),
+         "D2H next tokens");
     }
-    ck(cudaMemcpyAsync(c->h_stage + 2 * batch, c->tokens, sizeof(int) * batch, cudaMemcpyDeviceToHost, c->stream),
-       "D2H next tokens");
-    // the device error word rides along with the tokens (one synchronisation per step)
+    // the device error word rides along (one synchronisation per step)
     ck(cudaMemcpyAsync(c->h_stage + 3 * batch, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream),
        "D2H error word");
     if (logits_host)
@@ -1756,7 +1766,7 @@ int mmc_decode_step(mmc_ctx* c, int32_t batch, const int32_t* seq_ids, const int
          "D2H logits");
     ck(cudaStreamSynchronize(c->stream), "decode step");
     raise_device_error(c, c->h_stage[3 * batch]);
-    std::memcpy(next_tokens, c->h_stage + 2 * batch, sizeof(int) * batch);
+    std::memcpy(next_tokens, next_host, sizeof(int) * batch);
     for (int b = 0; b < batch; ++b) c->h_pos[seq_ids[b]] += 1;
   });
 }
@@ -1987,6 +1997,9 @@ int mmc_graph_build(mmc_ctx* c, int32_t batch, const int32_t* seq_ids) {
     ck(e, "graph instantiate");
     c->graph_batch = batch;
     c->graph_slots.assign(seq_ids, seq_ids + batch);
+    c->async_slots.assign(seq_ids, seq_ids + batch);  // uploaded above
+    ck(cudaMemsetAsync(c->hist_step, 0, kMaxParts * sizeof(int), c->stream), "history reset");
+    c->hist_host = 0;
     c->graph_cap_tokens = plan_cap_tokens(c, io);
   });
 }
@@ -1998,7 +2011,7 @@ int mmc_graph_set_tokens(mmc_ctx* c, const int32_t* tokens) {
     for (int b = 0; b < c->graph_batch; ++b)
       require(tokens[b] >= 0 && tokens[b] < c->d.vocab_size, MMC_ERR_OUT_OF_RANGE, "token id out of vocabulary range");
     upload(c, c->slots, c->graph_slots.data(), sizeof(int) * c->graph_batch, "slots");
-    c->async_slots.clear();
+    c->async_slots = c->graph_slots;
     upload(c, c->tokens, tokens, sizeof(int) * c->graph_batch, "tokens");
   });
 }
@@ -2020,6 +2033,7 @@ int mmc_graph_run(mmc_ctx* c, int32_t n_steps, void* stream) {
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
     ck(cudaMemsetAsync(c->hist_step, 0, kMaxParts * sizeof(int), st), "history reset");
     for (int i = 0; i < n_steps; ++i) ck(cudaGraphLaunch(c->graph, st), "graph launch");
+    c->hist_host = n_steps;
     for (int s : c->graph_slots) c->h_pos[s] += n_steps;
   });
 }
@@ -2044,6 +2058,7 @@ int mmc_graph_stream_start(mmc_ctx* c, int32_t n_steps) {
       for (auto& e : c->ring_ev) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "ring event");
     }
     ck(cudaMemsetAsync(c->hist_step, 0, kMaxParts * sizeof(int), c->stream), "history reset");
+    c->hist_host = 0;
     c->st_total = n_steps;
   });
 }
@@ -2057,6 +2072,7 @@ void stream_top_up(mmc_ctx* c) {
   while (c->st_enqueued < c->st_total && c->st_enqueued < c->st_consumed + kRingSlots) {
     const int slot = int(c->st_enqueued % kRingSlots);
     ck(cudaGraphLaunch(c->graph, c->stream), "graph launch");
+    ++c->hist_host;
     c->h_ring[slot] = 0;
     if (c->st_enqueued % 8 == 7 || c->st_enqueued + 1 == c->st_total)
       ck(cudaMemcpyAsync(c->h_ring + slot, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->stream), "D2H error word");
