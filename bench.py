@@ -448,10 +448,13 @@ def main() -> None:
                        "graph_replay_before": w["n_seqs"] * K / (graph_near_ms / 1000.0),
                        "path": "graph replays whose lm_head epilogue writes each step's tokens to mapped pinned host memory, read by the host "
                                "as they land (host wall clock, rank 0)"},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 8 * w["n_seqs"],
-                    "d2h_bytes_per_step": 4 * w["n_seqs"],
-                    "path": "mmc_decode_step (host token/sequence buffers -> pinned staging -> H2D, "
-                            "graph replay, D2H next tokens, synchronous)"},
+            # per step: the tokens go host -> device (the sequence list only when it changes, not in this
+            # loop); the next tokens come back through the argmax epilogue's write into mapped host memory,
+            # plus the device error word
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * w["n_seqs"],
+                    "d2h_bytes_per_step": 4 * w["n_seqs"] + 4,
+                    "path": "mmc_decode_step (host token buffer -> pinned staging -> H2D, graph replay, next tokens "
+                            "written to mapped host memory by the argmax epilogue, D2H error word, synchronous)"},
             "gpu_launches": kernels_per_step * K,
             "roofline": {
                 "bound": "hbm", "kernel": "persistent decode step (the whole step in one launch)",
