@@ -150,6 +150,11 @@ __device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, StageMeta&
 __device__ __forceinline__ void red_add_release_gpu(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -203,7 +208,7 @@ __global__ void __launch_bounds__(128) qk_prep_kernel(AttnArgs a) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(AttnArgs a) {
   using C = AttnCfg<HD>;
   extern __shared__ __align__(128) uint8_t smem[];
   __half* ring = reinterpret_cast<__half*>(smem);
@@ -215,11 +220,18 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
   __shared__ __align__(8) uint64_t full_bar[C::NST];
   __shared__ __align__(8) uint64_t empty_bar[C::NST];
   __shared__ StageMeta meta[C::NST];
-  __shared__ int merge_task, merge_ok;
+  __shared__ int merge_last, merge_task, merge_ok;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int total_items = a.max_splits * a.B * a.nkv;
 
+  // the queue words of an earlier launch that has completed (the previous
+  // layer's attention of this batch part): cleared here for its next use
+  if (a.work_prev != nullptr && blockIdx.x == 0 && tid == 0) {
+    a.work_prev[0] = 0u;
+    a.work_prev[1] = 0u;
+    a.work_prev[2] = 0u;
+  }
   if (tid == 0) {
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -553,18 +565,58 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
         }
       }
       consumer_sync();  // partials / outputs stored; comb is reused by the next item
-      // a split announces its partial without waiting: the merges run at the
-      // end of the kernel (below), off the page stream's critical path
-      if (it.nsplits > 1 && tid == 0) red_add_release_gpu(&a.counters[(size_t)it.b * a.nkv + it.h], 1u);
+      if (it.nsplits <= 1) continue;
+      if (a.merge_tail) {
+        // announce the partial without waiting: the merges run from the tail
+        // queue below, off the page stream's critical path
+        if (tid == 0) red_add_release_gpu(&a.counters[(size_t)it.b * a.nkv + it.h], 1u);
+        continue;
+      }
+      // the split that finishes last merges the (row, kv head)'s partials:
+      // no split waits for another
+      if (tid == 0) {
+        unsigned* cnt = &a.counters[(size_t)it.b * a.nkv + it.h];
+        __threadfence();
+        merge_last = atom_add_acq_rel_gpu(cnt, 1u) == unsigned(it.nsplits - 1);
+        if (merge_last) *cnt = 0u;  // every split has arrived: reset for the next launch
+      }
+      consumer_sync();
+      if (!merge_last) continue;
+      {
+        // stage the split partials in shared memory (independent coalesced
+        // loads), then merge from there
+        const int n = it.nsplits * int(pstride);
+        const bool staged = n <= int(C::comb_floats(rep));
+        if (staged) {
+          for (int i = tid; i < n; i += kConsumerWarps * 32) comb[i] = __ldcg(part_bh + i);
+          consumer_sync();
+        }
+        const float* src = staged ? comb : part_bh;
+        for (int i = tid; i < rep * HD; i += kConsumerWarps * 32) {
+          const int j = i / HD, d = i % HD;
+          float M = -1e30f;
+          for (int sp = 0; sp < it.nsplits; ++sp) M = fmaxf(M, src[sp * pstride + j * (HD + 2) + HD]);
+          float L = 0.f, O = 0.f;
+          for (int sp = 0; sp < it.nsplits; ++sp) {
+            const float* pp = src + sp * pstride + j * (HD + 2);
+            const float f = exp2f(pp[HD] - M);
+            L += pp[HD + 1] * f;
+            O += (staged ? pp[d] : __ldcg(pp + d)) * f;
+          }
+          put_out(j * HD + d, O / L);
+        }
+        consumer_sync();  // comb is reused by the next item
+      }
     }
 
     // ---------------------------------------------- tail: merge split items
-    // Once the work queue is empty every item is held by a running CTA, so
-    // waiting here for a (row, kv head)'s splits cannot deadlock. Tasks come
-    // from a second queue; each waits (bounded) for its pair's split count,
-    // merges the partials and clears the count.
-    const int pairs = a.B * a.nkv;
+    // (merge_tail) Once the work queue is empty every item is held by a
+    // running CTA, so waiting here for a (row, kv head)'s splits cannot
+    // deadlock. Tasks come from a second queue; each waits (bounded) for its
+    // pair's split count, merges the partials and clears the count.
+    const int pairs = a.merge_tail ? a.B * a.nkv : 0;
     for (;;) {
+      if (pairs == 0) break;
       if (tid == 0) merge_task = int(atomicAdd(&a.work[2], 1u));
       consumer_sync();
       const int task = merge_task;
@@ -595,8 +647,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
       if (merge_ok) {
         float* part_bh = a.part + ((size_t)b * a.nkv + h) * a.max_splits * pstride;
         const size_t out_off = (size_t)b * a.nq * HD + (size_t)h * rep * HD;
-        // stage the split partials in shared memory (independent coalesced
-        // loads), then merge from there
         const int n = nsplits * int(pstride);
         const bool staged = n <= int(C::comb_floats(rep));
         if (staged) {
@@ -613,7 +663,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
             const float* pp = src + sp * pstride + j * (HD + 2);
             const float f = exp2f(pp[HD] - M);
             L += pp[HD + 1] * f;
-            O += pp[d] * f;
+            O += (staged ? pp[d] : __ldcg(pp + d)) * f;
           }
           if (a.out16) a.out16[out_off + j * HD + d] = __float2half_rn(O / L);
           else a.out[out_off + j * HD + d] = O / L;
@@ -624,7 +674,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(AttnArgs a) 
     }
   }
 
-  // ---- queue reset: the last CTA to leave clears the work counters
+  // ---- queue reset: without a later launch that clears them, the last CTA
+  //      to leave clears the work counters
+  if (a.work_prev != nullptr) return;
   __syncthreads();
   if (tid == 0) {
     __threadfence();

@@ -233,7 +233,16 @@ struct AttnArgs {
   __half* out16 = nullptr;  // [B][nq * hd] fp16 when set (tensor-core path)
   float* part = nullptr;  // [B][nkv][max_splits][rep][hd + 2] split partials
   unsigned* counters = nullptr;  // [B][nkv], zero-initialised, self-resetting
-  unsigned* work = nullptr;      // [3] work-queue head, exit count, merge-queue head; zeroed, self-resetting
+  unsigned* work = nullptr;      // [3] work-queue head, exit count, merge-queue head; zeroed
+  // split merges: 0 = the split that finishes last merges its (row, kv head)
+  // at once; 1 = splits only announce their partials and the merges run from
+  // a tail queue once the work queue drains (keeps CTAs streaming pages when
+  // they hold several items)
+  int merge_tail = 0;
+  // optional [3]: the work words of an earlier launch that has completed (the
+  // previous layer's attention of the same batch part), which this launch
+  // clears; without it the last CTA of this launch clears its own words
+  unsigned* work_prev = nullptr;
   __half* q16 = nullptr;         // [B][nq][hd] fp16 normalised + rotated q (written by the prep launch)
   int ctas_per_sm = 0;           // persistent grid size per SM (0: 2)
   int* err = nullptr;

@@ -147,7 +147,7 @@ struct mmc_ctx {
   unsigned* argmax_counter = nullptr;
   float* attn_part = nullptr;
   unsigned* attn_counters = nullptr;
-  unsigned* attn_work = nullptr;  // [parts][4] attention work-queue words
+  unsigned* attn_work = nullptr;  // [parts][layers][4] attention work-queue words
   int decode_split_k = env_int("MMC_DECODE_SPLIT_K", 1);
   int decode_split_k_alone = env_int("MMC_DECODE_SPLIT_K_ALONE", 4);
   unsigned* chain_sync = nullptr;  // [parts][chain_sync_words(max_batch)] projection-chain queues
@@ -543,7 +543,22 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     a.out16 = tc ? attn16 : nullptr;
     a.part = attn_part;
     a.counters = attn_counters;
-    a.work = c->attn_work + 4 * io.part;
+    // one set of queue words per (batch part, layer); each launch clears the
+    // previous layer's set, which has completed by then (it is 4 launches back
+    // in the part's chain)
+    {
+      const int L = int(d.num_hidden_layers);
+      a.work = c->attn_work + 4 * (size_t(io.part) * L + l);
+      if (L > 1) a.work_prev = c->attn_work + 4 * (size_t(io.part) * L + (l + L - 1) % L);
+    }
+    // split merges (measured on B200): inline by the last split below 48 rows
+    // (batch 1 at 128..1152 positions: 290 vs 306 us per step), from the tail
+    // queue from 48 rows up, where CTAs hold several items (64 rows: 0.861 vs
+    // 0.894 ms, 128 rows: 1.157 vs 1.207 ms)
+    {
+      static const int mt = env_int("MMC_ATTN_MERGE_TAIL", -1);
+      a.merge_tail = mt >= 0 ? mt : (io.B >= 48 ? 1 : 0);
+    }
     a.q16 = c->q16 + r0 * Q;
     a.ctas_per_sm = io.attn_ctas_per_sm;
     a.err = c->err;
@@ -1548,7 +1563,8 @@ int mmc_kv_init(mmc_ctx* c, int64_t n_pages, int32_t max_seqs, int32_t max_batch
         mmc::attn_part_floats(max_batch, int(d.num_key_value_heads), c->max_splits_cap, c->rep(), int(d.head_dim)),
         "attention partials");
     c->attn_counters = c->alloc<unsigned>(size_t(max_batch) * d.num_key_value_heads, "attention counters");
-    c->attn_work = c->alloc<unsigned>(4 * kMaxParts, "attention work queues (per batch part)");
+    c->attn_work = c->alloc<unsigned>(4 * size_t(kMaxParts) * d.num_hidden_layers,
+                                      "attention work queues (per batch part and layer)");
     c->chain_words = mmc::chain_sync_words(max_batch);
     c->chain_sync = c->alloc<unsigned>(size_t(kMaxParts) * c->chain_words, "projection-chain queues (per batch part)");
     c->ss_cap = int(std::max<int64_t>((H + 127) / 128, mmc::skinny_grid(int(H), c->num_sms)));
