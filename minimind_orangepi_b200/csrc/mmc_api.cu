@@ -158,6 +158,7 @@ struct mmc_ctx {
   // persistent step (batches of up to kStepMaxRows rows, dense models)
   bool persistent = false;  // MMC_PERSISTENT at creation (default off: measured slower than the chain)
   bool skinny = true;       // MMC_SKINNY at creation: small batches on the skinny.cu projections
+  int attn_merge_tail = -1;  // MMC_ATTN_MERGE_TAIL at creation (-1: by batch size)
   int skinny_min_rows = env_int("MMC_SKINNY_MIN_ROWS", 2);  // smallest batch on them (1 row: gemv measured faster)
   __half* lm_s = nullptr;   // lm_head in the skinny fragment order
   int ss_cap = 0;           // sums-of-squares slots per row (the larger of the two paths' producers)
@@ -555,10 +556,7 @@ void enqueue_step(mmc_ctx* c, const StepIO& io, cudaStream_t s, cudaEvent_t* ev 
     // (batch 1 at 128..1152 positions: 290 vs 306 us per step), from the tail
     // queue from 48 rows up, where CTAs hold several items (64 rows: 0.861 vs
     // 0.894 ms, 128 rows: 1.157 vs 1.207 ms)
-    {
-      static const int mt = env_int("MMC_ATTN_MERGE_TAIL", -1);
-      a.merge_tail = mt >= 0 ? mt : (io.B >= 48 ? 1 : 0);
-    }
+    a.merge_tail = c->attn_merge_tail >= 0 ? c->attn_merge_tail : (io.B >= 48 ? 1 : 0);
     a.q16 = c->q16 + r0 * Q;
     a.ctas_per_sm = io.attn_ctas_per_sm;
     a.err = c->err;
@@ -1344,6 +1342,7 @@ int mmc_create(const mmc_model_desc* desc, int device, mmc_ctx** out) {
     c->persistent = env_int("MMC_PERSISTENT", 0) != 0;
     c->attn_fused = env_int("MMC_ATTN_FUSED", 1) != 0;
     c->skinny = env_int("MMC_SKINNY", 1) != 0;
+    c->attn_merge_tail = env_int("MMC_ATTN_MERGE_TAIL", -1);
     c->step_trace_on = env_int("MMC_STEP_TRACE", 0) != 0;
     ck(mmc::step_init_attributes(), "persistent step attributes");
     ck(mmc::gemv_init_attributes(), "gemv attributes");
