@@ -20,7 +20,10 @@ from oracle.oracle import Oracle, ReferenceModel, ref_available, REF_CLI
 
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden"
-REFERENCE = Path(os.environ.get("MINIMIND_REFERENCE_ROOT", "/root/reference"))
+# the reference checkout: MINIMIND_REFERENCE_ROOT, else a `reference` directory
+# beside this repository's own directory (as the build looks for it)
+REFERENCE = Path(os.environ["MINIMIND_REFERENCE_ROOT"]) if os.environ.get("MINIMIND_REFERENCE_ROOT") else \
+    ROOT.parent / "reference"
 GOLDEN_CASES = ["tiny", "tiny-hd64", "tiny-hd96-page-cross", "cfg1-minimind2-small", "tiny-moe"]
 
 
