@@ -62,9 +62,11 @@ struct AttnCfg {
   static constexpr size_t RING_BYTES = NST * STAGE_BYTES;
   // per stage: the group's q heads; after the ring: warp partials [warps][rep][HD + 2]
   // per stage: the group's fp16 q heads (prepared by qk_prep_kernel), or,
-  // fused, the raw fp32 q heads and the raw k and v of the group's kv head
+  // fused, the raw fp32 q heads and the raw k and v of the group's kv head,
+  // then the item's RoPE cos / sin rows (HD / 2 each) and the q / k norm
+  // weights (HD each)
   __host__ __device__ static size_t q_bytes(int rep, bool fused) {
-    return fused ? size_t(rep + 2) * HD * 4 : size_t(rep) * HD * 2;
+    return fused ? size_t(rep + 5) * HD * 4 : size_t(rep) * HD * 2;
   }
   __host__ __device__ static size_t comb_floats(int rep) { return size_t(kConsumerWarps) * rep * (HD + 2); }
   // fused: the item's normalised + rotated q heads and new k, v rows (fp16)
@@ -352,13 +354,21 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(AttnArgs a) 
         const bool last_split = cur.tok_end == cur.pos + 1;
         // fused: raw q heads, plus raw k and v for the split holding the current position
         const uint32_t qbytes = a.fused ? uint32_t((rep + (last_split ? 2 : 0)) * HD * 4) : uint32_t(rep * HD * 2);
-        mbar_arrive_expect_tx(&full_bar[s], uint32_t(C::STAGE_BYTES) + (first ? qbytes : 0u));
+        // fused: the item's RoPE rows and norm weights ride along (they do not
+        // depend on the previous kernel, so they go out at once)
+        const uint32_t aux = (first && a.fused) ? uint32_t(3 * HD * 4) : 0u;
+        mbar_arrive_expect_tx(&full_bar[s], uint32_t(C::STAGE_BYTES) + (first ? qbytes : 0u) + aux);
         __half* dst = ring + (size_t)s * 2 * C::TILE;
         bulk_g2s(dst, a.kv_pool + page_slab(page, a.layer, a.layers, 0, a.nkv, cur.h, C::TILE), C::TILE * 2,
                  &full_bar[s]);
         bulk_g2s(dst + C::TILE, a.kv_pool + page_slab(page, a.layer, a.layers, 1, a.nkv, cur.h, C::TILE),
                  C::TILE * 2, &full_bar[s]);
         if (first && a.fused) {
+          float* ax = reinterpret_cast<float*>(qring + (size_t)s * qstride) + (rep + 2) * HD;
+          bulk_g2s(ax, a.rope_cos + (size_t)cur.pos * (HD / 2), uint32_t(HD / 2 * 4), &full_bar[s]);
+          bulk_g2s(ax + HD / 2, a.rope_sin + (size_t)cur.pos * (HD / 2), uint32_t(HD / 2 * 4), &full_bar[s]);
+          bulk_g2s(ax + HD, a.q_norm, uint32_t(HD * 4), &full_bar[s]);
+          bulk_g2s(ax + 2 * HD, a.k_norm, uint32_t(HD * 4), &full_bar[s]);
           if (waited) {
             issue_raw(s, cur);
           } else {
@@ -410,12 +420,14 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attention_kernel(AttnArgs a) 
           // v rows when the item holds the current position. (Every warp has
           // its previous item's q in registers: the merge synchronised them.)
           const float* raw = reinterpret_cast<const float*>(qs);
-          const float* cos_r = a.rope_cos + (size_t)it.pos * (HD / 2);
-          const float* sin_r = a.rope_sin + (size_t)it.pos * (HD / 2);
+          const float* cos_r = raw + (rep + 2) * HD;  // copied with the page
+          const float* sin_r = cos_r + HD / 2;
+          const float* qn = cos_r + HD;
+          const float* kn = cos_r + 2 * HD;
           for (int j = warp; j < rep; j += kConsumerWarps)
-            norm_rope_head<HD>(raw + j * HD, a.q_norm, cos_r, sin_r, a.eps, prep + j * HD, lane);
+            norm_rope_head<HD>(raw + j * HD, qn, cos_r, sin_r, a.eps, prep + j * HD, lane);
           if (it.tok_end == it.pos + 1) {
-            if (warp == 0) norm_rope_head<HD>(raw + rep * HD, a.k_norm, cos_r, sin_r, a.eps, prep + rep * HD, lane);
+            if (warp == 0) norm_rope_head<HD>(raw + rep * HD, kn, cos_r, sin_r, a.eps, prep + rep * HD, lane);
             if (warp == 1)
               for (int d = lane; d < HD; d += 32) prep[(rep + 1) * HD + d] = __float2half_rn(raw[(rep + 1) * HD + d]);
           }
