@@ -25,10 +25,13 @@
 //   O^T[hd x 8 heads] += V^T[hd x 16 tok] . P^T  (ldmatrix.trans for V^T)
 // The GQA group's q heads sit on the mma N dimension, so one K/V read serves
 // all of them. At an item's last page the consumers merge their warps and
-// either write the output or a split partial; the last split to finish a
-// (row, kv head) merges the partials (arrival counter, self-resetting). The
-// producer never waits on the consumers except for a free stage, so copies
-// stay in flight across item boundaries.
+// either write the output or a split partial; the partials of a (row, kv
+// head) are merged by the split that arrives last at its counter
+// (self-resetting), or -- AttnArgs::merge_tail, for batches where CTAs hold
+// several items -- from a tail queue once the work queue drains. The queue
+// words of one launch are cleared by a later launch (AttnArgs::work_prev), so
+// no CTA ends with an atomic. The producer never waits on the consumers
+// except for a free stage, so copies stay in flight across item boundaries.
 //
 // Rows inside a page are stored with a 16-byte-chunk XOR swizzle (common.cuh
 // swz_chunk) so the flat page copy lands in shared memory already
